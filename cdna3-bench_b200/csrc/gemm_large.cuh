@@ -1,0 +1,283 @@
+// Large-M MXFP4 x BF16 GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// C[M, N] = A[M, K] (bf16) * dequant(W)^T with W the prepacked MXFP4 weights (N rows).
+//
+// The MMA computes the transposed product D = W_tile * A_tile^T so that the operand that
+// must be dequantised (the weights) is the MMA's "A" operand:
+//   * UMMA M = 128 weight rows (one prepacked chunk row block), UMMA N = 256 activation
+//     rows, K = 64 per pipeline stage (4 MMAs of K = 16).
+//   * Activations: TMA tiled load [256 rows x 64 k] bf16, 128-byte swizzle, K-major smem
+//     operand (the UMMA "B" operand).
+//   * Weights: one 4352-byte chunk per stage by a 1-D bulk copy; eight dequant warps expand
+//     it to bf16 exactly (table lookup, see common.cuh) and write it either
+//       kTS = true : into tensor memory with tcgen05.st (the MMA reads A from TMEM, which
+//                    keeps the dequantised tile off the shared-memory bandwidth), or
+//       kTS = false: into a 128B-swizzled K-major smem tile (classic SS MMA).
+//   * Accumulator: 128 lanes x 256 f32 columns of TMEM; the epilogue reads it with
+//     tcgen05.ld, converts to the output type, stages 32-row slabs in smem and writes
+//     them with TMA tensor stores.
+//   * Persistent CTAs (one per SM) walk the tile list in a grouped raster order.
+//
+// Warp roles (448 threads): 0 = TMA producer, 1 = MMA issuer (+TMEM owner),
+// 2..5 = epilogue (one per TMEM lane quarter), 6..13 = dequant (two per lane quarter,
+// one per 32-element half of the stage).
+#pragma once
+
+#include "common.cuh"
+
+namespace mxb {
+
+constexpr int kTcThreads = 448;
+constexpr int kTcTileAct = 256;  // activation rows per tile (UMMA N)
+constexpr int kTcTileW = 128;    // weight rows per tile (UMMA M)
+constexpr int kTcBK = 64;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemAccCol = 0;
+constexpr uint32_t kTmemARingCol = 256;
+
+template <bool kTS, typename OutT>
+struct TcCfg {
+  static constexpr int kStages = kTS ? 5 : 3;
+  static constexpr int kActBytes = kTcTileAct * kTcBK * 2;          // 32 KiB
+  static constexpr int kATileBytes = kTS ? 0 : kTcTileW * kTcBK * 2;  // 16 KiB (SS only)
+  static constexpr int kOutSlabBytes = 32 * kTcTileW * static_cast<int>(sizeof(OutT));
+  static constexpr int kOffA = kStages * kActBytes;
+  static constexpr int kOffOut = kOffA + kStages * kATileBytes;
+  static constexpr int kOffW = kOffOut + 2 * kOutSlabBytes;
+  static constexpr int kOffBar = kOffW + kStages * kChunkBytes;
+  static constexpr int kNumBars = 3 * kStages + 2;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;  // + slack for 1024-byte alignment
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ void tc_tile_coords(int t, int m_blocks, int n_blocks, int& mb, int& nb) {
+  constexpr int kGroupM = 8;  // raster: 8 activation blocks share the weight stream
+  const int per_group = kGroupM * n_blocks;
+  const int grp = t / per_group;
+  const int first = grp * kGroupM;
+  const int gm = min(m_blocks - first, kGroupM);
+  const int local = t - grp * per_group;
+  mb = first + local % gm;
+  nb = local / gm;
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT f32_bits_to(uint32_t v);
+template <>
+__device__ __forceinline__ float f32_bits_to<float>(uint32_t v) { return __uint_as_float(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 f32_bits_to<__nv_bfloat16>(uint32_t v) {
+  return __float2bfloat16_rn(__uint_as_float(v));
+}
+
+template <bool kTS, typename OutT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_out,
+                   const uint8_t* __restrict__ wpack, int M, int k_blocks, int m_blocks, int n_blocks) {
+  using Cfg = TcCfg<kTS, OutT>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* dqd = full + S;
+  uint64_t* empty = dqd + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = m_blocks * n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&dqd[s], 8);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_act);
+    prefetch_tmap(&tm_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, pend = 0, pend_ph = 0;
+      bool aborted = false;
+      for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
+        int mb, nb;
+        tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
+        const uint8_t* wsrc = wpack + static_cast<size_t>(nb) * k_blocks * kChunkBytes;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
+            aborted = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::kActBytes + kChunkBytes);
+          tma_load_2d(smem + s * Cfg::kActBytes, &tm_act, &full[s], kb * kTcBK, mb * kTcTileAct);
+          bulk_load(smem + Cfg::kOffW + s * kChunkBytes, wsrc + static_cast<size_t>(kb) * kChunkBytes,
+                    kChunkBytes, &full[s]);
+          pend |= 1u << s;
+          pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (aborted) {  // let every copy we started land before the CTA can exit
+        for (int i = 0; i < S; ++i)
+          if ((pend >> i) & 1) mbar_wait_drain(&full[i], (pend_ph >> i) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kTcTileW, kTcTileAct);
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      bool aborted = false, issued = false;
+      for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
+        if (!mbar_wait(acc_empty, aph ^ 1, kErrWaitAccEmpty, abort_flag)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag) ||
+              !mbar_wait(&dqd[s], ph, kErrWaitDequant, abort_flag)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(smem + s * Cfg::kActBytes));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint32_t acc = (kb | i) != 0;
+            if constexpr (kTS) {
+              mma_ts(tmem + kTmemAccCol, tmem + kTmemARingCol + s * 32 + i * 8, bdesc + 2 * i, idesc, acc);
+            } else {
+              const uint64_t adesc = umma_desc_sw128(smem_u32(smem + Cfg::kOffA + s * Cfg::kATileBytes));
+              mma_ss(tmem + kTmemAccCol, adesc + 2 * i, bdesc + 2 * i, idesc, acc);
+            }
+          }
+          issued = true;
+          tc_commit(&empty[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (aborted) break;
+        tc_commit(acc_full);
+        aph ^= 1;
+      }
+      if (aborted && issued) {  // wait for the MMAs already issued before TMEM is released
+        tc_commit(acc_full);
+        mbar_wait_drain(acc_full, aph);
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const bool leader = threadIdx.x == 64;
+    uint32_t aph = 0;
+    int slab = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int mb, nb;
+      tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
+      if (!warp_wait(acc_full, aph, kErrWaitAccFull, abort_flag)) break;
+      tc_fence_after();
+      const int m0 = mb * kTcTileAct;
+      const int live = min(kTcTileAct / 32, ceil_div(M - m0, 32));
+      for (int c = 0; c < live; ++c) {
+        const int buf = slab & 1;
+        ++slab;
+        if (leader) bulk_wait_read<1>();
+        named_bar_sync(1, 128);
+        uint32_t v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemAccCol + c * 32, v);
+        tmem_wait_ld();
+        if (c == live - 1) {  // whole accumulator read: hand TMEM back to the MMA issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty);
+        }
+        OutT* st = reinterpret_cast<OutT*>(smem + Cfg::kOffOut + buf * Cfg::kOutSlabBytes);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) st[j * kTcTileW + 32 * q + lane] = f32_bits_to<OutT>(v[j]);
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (leader) {
+          tma_store_2d(&tm_out, st, nb * kTcTileW, m0 + c * 32);
+          bulk_commit();
+        }
+      }
+      aph ^= 1;
+    }
+    if (leader) bulk_wait_all();
+  } else {
+    // ------------------------------------------------------------ dequant
+    const int q = warp & 3;
+    const int h = (warp - 6) >> 2;  // which 32-element group of the stage
+    const int r = 32 * q + lane;    // weight row inside the tile == TMEM lane
+    int s = 0;
+    uint32_t ph = 0;
+    bool aborted = false;
+    for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
+          aborted = true;
+          break;
+        }
+        const uint8_t* wst = smem + Cfg::kOffW + s * kChunkBytes;
+        const uint4 d = *reinterpret_cast<const uint4*>(wst + h * (kChunkRows * 16) + r * 16);
+        uint32_t v[16];
+        dequant_rowgroup(d, wst[kChunkData + h * kChunkRows + r], v);
+        if constexpr (kTS) {
+          tc_fence_after();
+          tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemARingCol + s * 32 + h * 16, v);
+          tmem_wait_st();
+          tc_fence_before();
+        } else {
+          uint8_t* at = smem + Cfg::kOffA + s * Cfg::kATileBytes + r * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(at + (((4 * h + j) ^ (r & 7)) << 4)) =
+                make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dqd[s]);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace mxb

@@ -1,0 +1,381 @@
+// C ABI of the library: argument checking, path selection, launches.
+// Single translation unit: the kernels live in the included .cuh files.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/mxfp4_b200.h"
+#include "common.cuh"
+#include "gemm_large.cuh"
+#include "gemm_small.cuh"
+#include "quant.cuh"
+
+namespace mxb {
+namespace {
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int ret(cudaError_t e) { return e == cudaSuccess ? 0 : static_cast<int>(e); }
+
+inline int launch_status() { return ret(cudaGetLastError()); }
+
+struct DeviceState {
+  int sm_count = 0;
+  int major = 0;
+  bool tc_attr[4] = {false, false, false, false};
+  bool gv_attr[4] = {false, false, false, false};
+};
+
+constexpr int kMaxDevices = 64;
+DeviceState g_dev[kMaxDevices];
+std::mutex g_mu;
+
+int current_device(DeviceState** st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ret(e);
+  if (dev < 0 || dev >= kMaxDevices) return MXFP4_ERR_DEVICE;
+  DeviceState& d = g_dev[dev];
+  if (d.sm_count == 0) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (d.sm_count == 0) {
+      int sms = 0, major = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+      if (e != cudaSuccess) return ret(e);
+      d.major = major;
+      d.sm_count = sms;
+    }
+  }
+  if (d.major != 10) return MXFP4_ERR_DEVICE;
+  *st = &d;
+  return 0;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return MXFP4_ERR_DRIVER;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
+}
+
+inline int k_blocks_of(int K) { return ceil_div(K, kChunkK); }
+inline int n_blocks_of(int N) { return ceil_div(N, kChunkRows); }
+
+// ------------------------------------------------------------------ large-M launch
+template <bool kTS, typename OutT>
+int launch_tc(const void* A, const uint8_t* wpack, void* C, int M, int N, int K, cudaStream_t stream,
+              DeviceState* d) {
+  using Cfg = TcCfg<kTS, OutT>;
+  const int slot = (kTS ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
+  if (!d->tc_attr[slot]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<kTS, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return ret(e);
+    d->tc_attr[slot] = true;
+  }
+  CUtensorMap tm_act, tm_out;
+  int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, kTcBK, kTcTileAct,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&tm_out,
+                 sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                 static_cast<int>(sizeof(OutT)), C, N, M, kTcTileW, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  const int m_blocks = ceil_div(M, kTcTileAct);
+  const int n_blocks = n_blocks_of(N);
+  const int tiles = m_blocks * n_blocks;
+  const int grid = std::min(tiles, d->sm_count);
+  gemm_tc_kernel<kTS, OutT><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(tm_act, tm_out, wpack, M,
+                                                                           k_blocks_of(K), m_blocks, n_blocks);
+  return launch_status();
+}
+
+// ------------------------------------------------------------------ small-M launch
+struct GvPlan {
+  int nt, ks, kbps, smem;
+};
+
+GvPlan plan_gemv(int M, int N, int K, int sm_count) {
+  GvPlan p;
+  p.nt = M <= 8 ? 1 : 2;
+  const int nb = n_blocks_of(N), kb = k_blocks_of(K);
+  const int x_per_kb = 2 * (8 * p.nt) * 64;
+  const int fixed = p.nt == 1 ? GvCfg<1>::kOffX : GvCfg<2>::kOffX;
+  p.ks = 1;
+  // enough CTAs to cover every SM twice, and the staged activations within ~96 KiB
+  while (p.ks < 8 && (nb * p.ks < 2 * sm_count || ceil_div(kb, p.ks) * x_per_kb > 96 * 1024)) p.ks *= 2;
+  p.kbps = ceil_div(kb, p.ks);
+  p.smem = fixed + p.kbps * x_per_kb;
+  return p;
+}
+
+template <int NT, typename OutT>
+int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, int K, const GvPlan& p,
+                  cudaStream_t stream, DeviceState* d) {
+  const int slot = (NT == 1 ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
+  if (!d->gv_attr[slot]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         232448 - 1024);
+    if (e != cudaSuccess) return ret(e);
+    d->gv_attr[slot] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_blocks_of(N), p.ks, 1);
+  cfg.blockDim = dim3(kGvThreads, 1, 1);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.ks;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, OutT>, static_cast<const __nv_bfloat16*>(A), M, K,
+                                     wpack, k_blocks_of(K), p.kbps, static_cast<OutT*>(C), N);
+  return ret(e);
+}
+
+int launch_gemv(const void* A, const uint8_t* wpack, void* C, int c_dtype, int M, int N, int K,
+                cudaStream_t stream, DeviceState* d) {
+  const GvPlan p = plan_gemv(M, N, K, d->sm_count);
+  if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (p.nt == 1)
+    return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<1, float>(A, wpack, C, M, N, K, p, stream, d)
+                                      : launch_gemv_t<1, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d);
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<2, float>(A, wpack, C, M, N, K, p, stream, d)
+                                    : launch_gemv_t<2, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d);
+}
+
+size_t prepacked_bytes(int N, int K) {
+  return static_cast<size_t>(n_blocks_of(N)) * k_blocks_of(K) * kChunkBytes;
+}
+
+int do_prepack(const uint8_t* packed, const uint8_t* scales, int N, int K, int layout, uint8_t* dst,
+               cudaStream_t stream) {
+  const int kb = k_blocks_of(K), nb = n_blocks_of(N);
+  const long long total = static_cast<long long>(nb) * kb * 2 * kChunkRows;
+  const int threads = 256;
+  prepack_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, stream>>>(
+      packed, scales, N, K, layout, kb, nb, dst);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace mxb
+
+using namespace mxb;
+
+extern "C" {
+
+int mxfp4_abi_version(void) { return MXFP4_B200_ABI_VERSION; }
+
+int mxfp4_device_info_get(int device, mxfp4_device_info* out) {
+  if (!out) return MXFP4_ERR_INVALID_ARGUMENT;
+  cudaDeviceProp p;
+  cudaError_t e = cudaGetDeviceProperties(&p, device);
+  if (e != cudaSuccess) return ret(e);
+  std::memset(out, 0, sizeof(*out));
+  std::strncpy(out->name, p.name, sizeof(out->name) - 1);
+  out->major = p.major;
+  out->minor = p.minor;
+  out->multi_processor_count = p.multiProcessorCount;
+  out->warp_size = p.warpSize;
+  out->total_global_mem = static_cast<long long>(p.totalGlobalMem);
+  out->shared_mem_per_block = static_cast<long long>(p.sharedMemPerBlock);
+  out->shared_mem_per_block_optin = static_cast<long long>(p.sharedMemPerBlockOptin);
+  out->l2_cache_size = p.l2CacheSize;
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrClockRate, device) == cudaSuccess) out->clock_rate_khz = v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMemoryClockRate, device) == cudaSuccess) out->memory_clock_rate_khz = v;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrGlobalMemoryBusWidth, device) == cudaSuccess) out->memory_bus_width = v;
+  return 0;
+}
+
+int mxfp4_device_error(int clear, unsigned int* code_out) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_mxfp4_error, sizeof(v));
+  if (e != cudaSuccess) return ret(e);
+  if (clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_mxfp4_error, &z, sizeof(z));
+    if (e != cudaSuccess) return ret(e);
+  }
+  if (code_out) *code_out = v;
+  return 0;
+}
+
+const char* mxfp4_error_string(int code) {
+  switch (code) {
+    case 0: return "success";
+    case MXFP4_ERR_INVALID_ARGUMENT: return "mxfp4: invalid argument";
+    case MXFP4_ERR_UNSUPPORTED_SHAPE: return "mxfp4: shape not supported by the selected path";
+    case MXFP4_ERR_MISALIGNED: return "mxfp4: pointer or row stride not 16-byte aligned";
+    case MXFP4_ERR_WORKSPACE: return "mxfp4: workspace missing or too small";
+    case MXFP4_ERR_DRIVER: return "mxfp4: tensor-map encoder unavailable or rejected the tensor";
+    case MXFP4_ERR_DEVICE: return "mxfp4: current device is not an sm_100 GPU";
+    default: return cudaGetErrorString(static_cast<cudaError_t>(code));
+  }
+}
+
+int mxfp4_quantize(const float* x, int rows, int cols, int axis, int rule, uint8_t* packed, uint8_t* scales,
+                   void* stream) {
+  if (!x || !packed || !scales || rows <= 0 || cols <= 0 || (axis != 0 && axis != 1) || (rule != 0 && rule != 1))
+    return MXFP4_ERR_INVALID_ARGUMENT;
+  const int qlen = axis == 0 ? rows : cols;
+  if (qlen % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (axis == 1 && !aligned16(x)) return MXFP4_ERR_MISALIGNED;
+  if (axis == 1 && !aligned16(packed)) return MXFP4_ERR_MISALIGNED;
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long work = static_cast<long long>(rows / (axis == 0 ? kGroup : 1)) * (cols / (axis == 0 ? 1 : kGroup));
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((work + threads - 1) / threads);
+  if (axis == 0) {
+    if (rule == 0) quantize_axis0_kernel<0><<<blocks, threads, 0, s>>>(x, rows, cols, packed, scales);
+    else quantize_axis0_kernel<1><<<blocks, threads, 0, s>>>(x, rows, cols, packed, scales);
+  } else {
+    if (rule == 0) quantize_axis1_kernel<0><<<blocks, threads, 0, s>>>(x, rows, cols, packed, scales);
+    else quantize_axis1_kernel<1><<<blocks, threads, 0, s>>>(x, rows, cols, packed, scales);
+  }
+  return launch_status();
+}
+
+int mxfp4_dequantize(const uint8_t* packed, const uint8_t* scales, int K, int N, int layout, void* out,
+                     int out_dtype, void* stream) {
+  if (!packed || !scales || !out || K <= 0 || N <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if ((layout != MXFP4_LAYOUT_REF && layout != MXFP4_LAYOUT_NK) || (out_dtype != 0 && out_dtype != 1))
+    return MXFP4_ERR_INVALID_ARGUMENT;
+  auto s = static_cast<cudaStream_t>(stream);
+  const long long work = static_cast<long long>(K / 2) * N;
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((work + threads - 1) / threads);
+  if (layout == MXFP4_LAYOUT_REF) {
+    if (out_dtype == MXFP4_DTYPE_F32)
+      dequant_ref_kernel<float><<<blocks, threads, 0, s>>>(packed, scales, K, N, static_cast<float*>(out));
+    else
+      dequant_ref_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(packed, scales, K, N,
+                                                                   static_cast<__nv_bfloat16*>(out));
+  } else {
+    if (out_dtype == MXFP4_DTYPE_F32)
+      dequant_nk_kernel<float><<<blocks, threads, 0, s>>>(packed, scales, K, N, static_cast<float*>(out));
+    else
+      dequant_nk_kernel<__nv_bfloat16><<<blocks, threads, 0, s>>>(packed, scales, K, N,
+                                                                  static_cast<__nv_bfloat16*>(out));
+  }
+  return launch_status();
+}
+
+size_t mxfp4_prepacked_bytes(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  return prepacked_bytes(N, K);
+}
+
+int mxfp4_prepack(const uint8_t* packed, const uint8_t* scales, int N, int K, int src_layout, uint8_t* dst,
+                  void* stream) {
+  if (!packed || !scales || !dst || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (src_layout != MXFP4_LAYOUT_REF && src_layout != MXFP4_LAYOUT_NK && src_layout != MXFP4_LAYOUT_G)
+    return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (src_layout == MXFP4_LAYOUT_G && (N % 128 || K % 8)) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(dst)) return MXFP4_ERR_MISALIGNED;
+  return do_prepack(packed, scales, N, K, src_layout, dst, static_cast<cudaStream_t>(stream));
+}
+
+int mxfp4_dequantize_prepacked(const uint8_t* wpack, int N, int K, uint16_t* out, void* stream) {
+  if (!wpack || !out || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(wpack) || !aligned16(out)) return MXFP4_ERR_MISALIGNED;
+  const int kb = k_blocks_of(K), nb = n_blocks_of(N);
+  const long long total = static_cast<long long>(nb) * kb * 2 * kChunkRows;
+  const int threads = 256;
+  dequant_prepacked_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0,
+                             static_cast<cudaStream_t>(stream)>>>(wpack, N, K, kb, nb, out);
+  return launch_status();
+}
+
+int mxfp4_select_path(int M, int N, int K) {
+  (void)N;
+  (void)K;
+  // Decode shapes are weight-streaming bound; the tcgen05 tile is 256 activation rows wide
+  // and would waste >90% of its MMA work below 17 rows.
+  return M <= 16 ? MXFP4_PATH_GEMV : MXFP4_PATH_TC;
+}
+
+int mxfp4_shape_supported(int path, int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % kGroup || N % 8) return 0;
+  switch (path) {
+    case MXFP4_PATH_AUTO: return 1;
+    case MXFP4_PATH_TC:
+    case MXFP4_PATH_TC_SMEM: return 1;
+    case MXFP4_PATH_GEMV: return M <= 16 ? 1 : 0;
+    default: return 0;
+  }
+}
+
+size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
+  (void)M;
+  if (N <= 0 || K <= 0) return 0;
+  return layout == MXFP4_LAYOUT_PREPACKED ? 0 : prepacked_bytes(N, K);
+}
+
+int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype, int M, int N,
+               int K, int layout, int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (c_dtype != MXFP4_DTYPE_F32 && c_dtype != MXFP4_DTYPE_BF16) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (layout < MXFP4_LAYOUT_REF || layout > MXFP4_LAYOUT_PREPACKED) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (path < MXFP4_PATH_AUTO || path > MXFP4_PATH_GEMV) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (layout != MXFP4_LAYOUT_PREPACKED && !B_scales) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (path == MXFP4_PATH_AUTO) path = mxfp4_select_path(M, N, K);
+  if (!mxfp4_shape_supported(path, M, N, K)) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(A) || !aligned16(C) || !aligned16(B)) return MXFP4_ERR_MISALIGNED;
+  DeviceState* d = nullptr;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  const uint8_t* wpack = B;
+  if (layout != MXFP4_LAYOUT_PREPACKED) {
+    const size_t need = prepacked_bytes(N, K);
+    if (!workspace || workspace_bytes < need) return MXFP4_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return MXFP4_ERR_MISALIGNED;
+    if (layout == MXFP4_LAYOUT_G && N % 128) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+    rc = do_prepack(B, B_scales, N, K, layout, static_cast<uint8_t*>(workspace), s);
+    if (rc) return rc;
+    wpack = static_cast<const uint8_t*>(workspace);
+  }
+  switch (path) {
+    case MXFP4_PATH_TC:
+      return c_dtype == MXFP4_DTYPE_F32 ? launch_tc<true, float>(A, wpack, C, M, N, K, s, d)
+                                        : launch_tc<true, __nv_bfloat16>(A, wpack, C, M, N, K, s, d);
+    case MXFP4_PATH_TC_SMEM:
+      return c_dtype == MXFP4_DTYPE_F32 ? launch_tc<false, float>(A, wpack, C, M, N, K, s, d)
+                                        : launch_tc<false, __nv_bfloat16>(A, wpack, C, M, N, K, s, d);
+    case MXFP4_PATH_GEMV: return launch_gemv(A, wpack, C, c_dtype, M, N, K, s, d);
+    default: return MXFP4_ERR_INVALID_ARGUMENT;
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,137 @@
+/*
+ * mxfp4_b200 — C ABI of the B200 (sm_100a) MXFP4-weight x BF16-activation GEMM library.
+ *
+ * Plain pointers and sizes only.  Every device pointer must be 16-byte aligned and refer to
+ * contiguous row-major memory on the current CUDA device; `stream` is a cudaStream_t
+ * (NULL = legacy default stream).  All entry points are asynchronous on `stream`, allocate
+ * nothing, keep no per-call host state and are safe to call from several host threads.
+ * Return value: 0 on success, a cudaError_t value (1..999) for a CUDA error, or one of the
+ * MXFP4_ERR_* codes below; mxfp4_error_string() turns either into text.
+ *
+ * Data formats (identical bytes to the reference package mxfp4_cdna3):
+ *   E2M1 nibble = sign<<3 | magnitude index, magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6};
+ *   two nibbles per byte along K, even k in the low nibble;
+ *   one E8M0 scale byte per 32 K-elements, value 2**(byte - 127).
+ * Weight layouts accepted by the GEMM and the prepack:
+ *   MXFP4_LAYOUT_REF       B_packed uint8 [K/2, N], B_scales uint8 [K/32, N]
+ *                          (reference: csrc/mxfp4_ext.cpp:21-24, python/mxfp4_cdna3/ref.py:14-47)
+ *   MXFP4_LAYOUT_NK        W_packed uint8 [N, K/2], W_scales uint8 [N, K/32] (row-major weights)
+ *   MXFP4_LAYOUT_G         the reference's strategy-G prepack, flattened
+ *                          (python/mxfp4_cdna3/ref.py:85-101; needs N % 128 == 0)
+ *   MXFP4_LAYOUT_PREPACKED this library's chunk layout from mxfp4_prepack(); B_scales unused
+ */
+#ifndef MXFP4_B200_H_
+#define MXFP4_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MXFP4_B200_ABI_VERSION 1
+
+enum mxfp4_layout {
+  MXFP4_LAYOUT_REF = 0,
+  MXFP4_LAYOUT_NK = 1,
+  MXFP4_LAYOUT_G = 2,
+  MXFP4_LAYOUT_PREPACKED = 3
+};
+
+enum mxfp4_dtype { MXFP4_DTYPE_F32 = 0, MXFP4_DTYPE_BF16 = 1 };
+
+enum mxfp4_path {
+  MXFP4_PATH_AUTO = 0,     /* cost model picks (mxfp4_select_path) */
+  MXFP4_PATH_TC = 1,       /* large-M tcgen05 kernel, dequantised weights in tensor memory */
+  MXFP4_PATH_TC_SMEM = 2,  /* large-M tcgen05 kernel, dequantised weights in shared memory */
+  MXFP4_PATH_GEMV = 3      /* small-M (M <= 16) streaming kernel, cluster split-K */
+};
+
+enum mxfp4_quant_rule {
+  MXFP4_RULE_REF = 0, /* reference rule: ceil(log2(amax/6)), ties to the lower magnitude */
+  MXFP4_RULE_OCP = 1  /* OCP MX: floor(log2(amax)) - 2, round-nearest-even, saturate at 6 */
+};
+
+#define MXFP4_ERR_INVALID_ARGUMENT 1000 /* null pointer, negative size, bad enum */
+#define MXFP4_ERR_UNSUPPORTED_SHAPE 1001 /* shape outside what the chosen path handles */
+#define MXFP4_ERR_MISALIGNED 1002 /* pointer or row stride not 16-byte aligned */
+#define MXFP4_ERR_WORKSPACE 1003 /* workspace missing or smaller than required */
+#define MXFP4_ERR_DRIVER 1004 /* driver entry point (tensor-map encoder) unavailable */
+#define MXFP4_ERR_DEVICE 1005 /* current device is not an sm_100 part */
+
+typedef struct mxfp4_device_info {
+  char name[256];
+  int major, minor;
+  int multi_processor_count;
+  int warp_size;
+  long long total_global_mem;
+  long long shared_mem_per_block;
+  long long shared_mem_per_block_optin;
+  long long l2_cache_size;
+  int clock_rate_khz;
+  int memory_clock_rate_khz;
+  int memory_bus_width;
+} mxfp4_device_info;
+
+/* Library ABI version (MXFP4_B200_ABI_VERSION). */
+int mxfp4_abi_version(void);
+
+/* Device properties (replaces the reference's device_info, csrc/mxfp4_ext.cpp:156-168). */
+int mxfp4_device_info_get(int device, mxfp4_device_info* out);
+
+/* Reads the device error word that bounded waits inside the kernels set when they give up
+ * (0 = none); clears it when `clear` is non-zero.  Synchronises the device. */
+int mxfp4_device_error(int clear, unsigned int* code_out);
+
+const char* mxfp4_error_string(int code);
+
+/* Quantise fp32 x[rows, cols] along `axis` (0: groups of 32 rows -> packed [rows/2, cols],
+ * scales [rows/32, cols]; 1: groups of 32 columns -> [rows, cols/2], [rows, cols/32]).
+ * Replaces quantize_mxfp4 (python/mxfp4_cdna3/ref.py:14-47) for rule MXFP4_RULE_REF. */
+int mxfp4_quantize(const float* x, int rows, int cols, int axis, int rule, uint8_t* packed,
+                   uint8_t* scales, void* stream);
+
+/* Dequantise to fp32 or bf16.  layout MXFP4_LAYOUT_REF: [K/2,N]+[K/32,N] -> out [K,N];
+ * MXFP4_LAYOUT_NK: [N,K/2]+[N,K/32] -> out [N,K].
+ * Replaces dequantize_mxfp4 (python/mxfp4_cdna3/ref.py:50-72). */
+int mxfp4_dequantize(const uint8_t* packed, const uint8_t* scales, int K, int N, int layout,
+                     void* out, int out_dtype, void* stream);
+
+/* Bytes of the prepacked form of an N x K weight (N padded to 128, K to 64). */
+size_t mxfp4_prepacked_bytes(int N, int K);
+
+/* Re-lay weights (src_layout REF, NK or G) into the chunk layout the GEMM kernels stream.
+ * Replaces prepack_b_mxfp4 (python/mxfp4_cdna3/ref.py:85-101) as the B200 analogue of the
+ * strategy-G layout.  dst must hold mxfp4_prepacked_bytes(N, K) bytes. */
+int mxfp4_prepack(const uint8_t* packed, const uint8_t* scales, int N, int K, int src_layout,
+                  uint8_t* dst, void* stream);
+
+/* Dequantise prepacked weights to bf16 bit patterns out[N, K] with the exact table-lookup
+ * routine the tensor-core kernel uses (for bit-exact verification of the GEMM's tile). */
+int mxfp4_dequantize_prepacked(const uint8_t* wpack, int N, int K, uint16_t* out, void* stream);
+
+/* Path the cost model picks for C[M,N] = A[M,K] * dequant(B) (an mxfp4_path value). */
+int mxfp4_select_path(int M, int N, int K);
+
+/* 1 if `path` (MXFP4_PATH_*) handles the shape, else 0.  Replaces shape_supported_{c,d,e,f,g}
+ * (csrc/common.h:80-99): every path here needs K % 32 == 0 and N % 8 == 0. */
+int mxfp4_shape_supported(int path, int M, int N, int K);
+
+/* Workspace bytes mxfp4_gemm needs for a weight layout (0 for MXFP4_LAYOUT_PREPACKED; the
+ * prepacked copy of B for the other layouts). */
+size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout);
+
+/* C[M,N] = A[M,K] (bf16) * dequant(B)[K,N], fp32 accumulation, C in c_dtype.
+ * Replaces the launcher ABI launch_strategy_{a..m} (csrc/common.h:43-78) and the dispatch
+ * in csrc/mxfp4_ext.cpp:36-48; the reference always writes fp32 C, this adds bf16.
+ * For layouts other than PREPACKED the weights are first re-laid into `workspace`. */
+int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
+               int M, int N, int K, int layout, int path, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXFP4_B200_H_ */

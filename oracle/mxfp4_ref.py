@@ -1,0 +1,207 @@
+"""CPU oracle for the MXFP4 x BF16 GEMM path.  TEST INFRASTRUCTURE ONLY.
+
+This module restates, in NumPy, the reference package's CPU algorithm
+(konradha/cdna3-bench, ``python/mxfp4_cdna3/ref.py``).  It is the checker the
+parity tests compare the CUDA path against, and the timed CPU baseline of
+``bench.py``.  Nothing in the product package imports it; only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm do.
+
+Parity is pinned: ``tests/test_oracle.py`` checks every function here against
+golden vectors produced by importing the reference itself
+(``tests/golden/make_golden.py``) and against the reference's own known-answer
+tests (``tests/test_smoke.py`` of the reference: zero round trip, the
+``[4,-4]*16 -> scale 127 / bytes 0xE6`` bit layout).
+
+Formats (same bytes as the reference):
+  * E2M1 nibble = sign<<3 | magnitude index, magnitudes {0,.5,1,1.5,2,3,4,6}.
+  * Two nibbles per byte along the quantised axis: even element in the low
+    nibble, odd element in the high nibble.
+  * One E8M0 scale byte per 32 elements along the axis: value 2**(byte-127).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+GROUP = 32
+E2M1_MAGNITUDES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float32)
+
+# Decision boundaries between consecutive E2M1 magnitudes (midpoints).
+_MIDPOINTS = (E2M1_MAGNITUDES[1:] + E2M1_MAGNITUDES[:-1]) / 2.0
+
+
+def _groups_last(x: np.ndarray, axis: int) -> tuple[np.ndarray, tuple[int, ...]]:
+    x = np.moveaxis(x, axis, -1)
+    lead = x.shape[:-1]
+    if x.shape[-1] % GROUP:
+        raise ValueError(f"axis {axis} length {x.shape[-1]} not divisible by {GROUP}")
+    return x.reshape(*lead, x.shape[-1] // GROUP, GROUP), lead
+
+
+def _pack_nibbles(nib: np.ndarray, lead, n_groups: int, axis: int) -> np.ndarray:
+    nib = nib.reshape(*lead, n_groups * GROUP)
+    packed = (nib[..., 0::2] & 0xF) | ((nib[..., 1::2] & 0xF) << 4)
+    return np.ascontiguousarray(np.moveaxis(packed.astype(np.uint8), -1, axis))
+
+
+def _nearest_index_ties_low(mag: np.ndarray) -> np.ndarray:
+    """Index of the nearest E2M1 magnitude; an exact tie picks the LOWER one.
+
+    Follows ``_nearest_e2m1`` (ref.py:6-11): ``argmin`` of the absolute
+    difference returns the first (smallest) index on ties.  A value exactly on
+    a midpoint therefore maps down: ``searchsorted(side='left')`` counts the
+    midpoints strictly below ``mag``.
+    """
+    return np.searchsorted(_MIDPOINTS, mag, side="left").astype(np.uint8)
+
+
+def quantize_mxfp4(x, axis=-1):
+    """Reference quantiser (ref.py:14-47).
+
+    scale exponent = ceil(log2(max(amax, 1e-38) / 6)) clipped to [-127, 127];
+    elements are divided by 2**exp and mapped to the nearest E2M1 magnitude
+    with ties to the lower magnitude.  Returns (packed uint8, scales uint8)
+    with the quantised axis halved / divided by 32 respectively.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    g, lead = _groups_last(x, axis)
+    amax = np.max(np.abs(g), axis=-1)
+    e = np.clip(np.ceil(np.log2(np.maximum(amax, np.float32(1e-38)) / np.float32(6.0))), -127, 127)
+    e = e.astype(np.int32)
+    scaled = g / np.power(np.float32(2.0), e.astype(np.float32))[..., None]
+    idx = _nearest_index_ties_low(np.abs(scaled))
+    nib = idx | ((scaled < 0).astype(np.uint8) << 3)
+    scales = np.ascontiguousarray(np.moveaxis((e + 127).astype(np.uint8), -1, axis))
+    return _pack_nibbles(nib, lead, g.shape[-2], axis), scales
+
+
+def _rne_index(mag: np.ndarray) -> np.ndarray:
+    """Nearest E2M1 magnitude, ties to the even code (OCP MX round-to-nearest-even),
+    saturating at 6."""
+    lo = np.searchsorted(_MIDPOINTS, mag, side="left")  # ties -> lower
+    hi = np.searchsorted(_MIDPOINTS, mag, side="right")  # ties -> upper
+    tie = lo != hi
+    # on a tie the two candidates are lo (code lo) and hi = lo + 1; pick the even code
+    idx = np.where(tie & (lo % 2 == 1), hi, lo)
+    return np.minimum(idx, 7).astype(np.uint8)
+
+
+def quantize_mxfp4_ocp(x, axis=-1):
+    """OCP MX v1.0 E2M1 quantiser (the rule the benchmark configs name).
+
+    shared exponent = floor(log2(amax)) - 2 (2 = emax of E2M1), clipped to
+    [-127, 127]; an all-zero block gets exponent -127.  Elements are divided by
+    2**exp, rounded to nearest-even on the E2M1 grid and saturated at +-6.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    g, lead = _groups_last(x, axis)
+    amax = np.max(np.abs(g), axis=-1)
+    # floor(log2(amax)) computed exactly from the binary exponent (frexp: amax = m*2**E,
+    # m in [0.5, 1)), so blocks whose amax sits one ulp below a power of two are not
+    # rounded up by a float32 log2.
+    _, E = np.frexp(amax)
+    e = (E.astype(np.int64) - 1) - 2
+    e = np.where(amax > 0, e, -127)
+    e = np.clip(e, -127, 127).astype(np.int32)
+    scaled = g / np.power(np.float32(2.0), e.astype(np.float32))[..., None]
+    idx = _rne_index(np.abs(scaled))
+    nib = idx | ((scaled < 0).astype(np.uint8) << 3)
+    scales = np.ascontiguousarray(np.moveaxis((e + 127).astype(np.uint8), -1, axis))
+    return _pack_nibbles(nib, lead, g.shape[-2], axis), scales
+
+
+def dequantize_mxfp4(packed, scales, axis=-1):
+    """Reference dequantiser (ref.py:50-72): value = (+-)E2M1[em] * 2**(scale-127) in fp32."""
+    packed = np.moveaxis(np.asarray(packed, dtype=np.uint8), axis, -1)
+    scales = np.moveaxis(np.asarray(scales, dtype=np.uint8), axis, -1)
+    nib = np.empty((*packed.shape[:-1], packed.shape[-1] * 2), dtype=np.uint8)
+    nib[..., 0::2] = packed & 0xF
+    nib[..., 1::2] = packed >> 4
+    val = E2M1_MAGNITUDES[nib & 7] * np.where(nib & 8, np.float32(-1.0), np.float32(1.0))
+    with np.errstate(over="ignore", invalid="ignore"):
+        mult = np.power(2.0, scales.astype(np.int32) - 127).astype(np.float32)
+        lead = val.shape[:-1]
+        out = val.reshape(*lead, -1, GROUP) * mult[..., None]
+    return np.moveaxis(out.reshape(*lead, -1), -1, axis)
+
+
+def ref_gemm(A, B_packed, B_scales):
+    """Reference GEMM (ref.py:75-78): fp32 A @ dequant(B) with B = [K/2, N] / [K/32, N]."""
+    A = np.asarray(A)
+    A32 = A if A.dtype == np.float32 else A.astype(np.float32)
+    return A32 @ dequantize_mxfp4(B_packed, B_scales, axis=0)
+
+
+def preshuffle_b(B_packed, B_scales, N_tile=128, K_tile=128):
+    """Identity placeholder kept for interface parity (ref.py:81-82)."""
+    return np.ascontiguousarray(B_packed), np.ascontiguousarray(B_scales)
+
+
+def prepack_b_mxfp4(B_packed, B_scales, n_tile=128):
+    """Strategy-G prepack of the reference (ref.py:85-101).
+
+    B_prep[nb, K/8, n_tile, 4] (byte b of each 4-byte word = K-byte 4*chunk+b),
+    Bs_prep[nb, K/32, n_tile]; both returned flattened.
+    """
+    B_packed = np.ascontiguousarray(B_packed)
+    K2, N = B_packed.shape
+    if N % n_tile:
+        raise AssertionError("N must be a multiple of n_tile")
+    nb = N // n_tile
+    bp = B_packed.reshape(K2 // 4, 4, nb, n_tile).transpose(2, 0, 3, 1)
+    bs = np.ascontiguousarray(B_scales).reshape(-1, nb, n_tile).transpose(1, 0, 2)
+    return np.ascontiguousarray(bp).reshape(-1), np.ascontiguousarray(bs).reshape(-1)
+
+
+# --------------------------------------------------------------------------------------
+# Helpers for the B200 library's own formats (restated on the host for the tests).
+# --------------------------------------------------------------------------------------
+
+CHUNK_ROWS = 128  # weight rows (output columns n) per chunk
+CHUNK_K = 64  # K elements per chunk
+CHUNK_DATA = CHUNK_ROWS * CHUNK_K // 2  # 4096 bytes of nibbles
+CHUNK_BYTES = CHUNK_DATA + CHUNK_ROWS * (CHUNK_K // GROUP)  # + 256 scale bytes = 4352
+
+
+def b200_prepack(B_packed, B_scales):
+    """Host restatement of the B200 prepacked weight layout (the GPU prepack's oracle).
+
+    Input: reference layout B_packed [K/2, N], B_scales [K/32, N].  N is padded to
+    a multiple of 128 and K to a multiple of 64 with zero nibbles and scale 127.
+    Output: uint8 [N_pad/128, K_pad/64, 4352] where each 4352-byte chunk is
+      data  [g in 0..1][r in 0..127][16 bytes]   (g = 32-element group of the chunk)
+      scale [g in 0..1][r in 0..127]
+    and inside a row-group the 16 bytes are ordered so that 4-byte word w holds
+    the k-pairs {w, w+4, w+8, w+12} (byte b of word w = k-pair w + 4*b).
+    """
+    B_packed = np.asarray(B_packed, dtype=np.uint8)
+    B_scales = np.asarray(B_scales, dtype=np.uint8)
+    K2, N = B_packed.shape
+    K = 2 * K2
+    Np = -(-N // CHUNK_ROWS) * CHUNK_ROWS
+    Kp = -(-K // CHUNK_K) * CHUNK_K
+    bp = np.zeros((Kp // 2, Np), dtype=np.uint8)
+    bp[:K2, :N] = B_packed
+    bs = np.full((Kp // GROUP, Np), 127, dtype=np.uint8)
+    bs[: K // GROUP, :N] = B_scales
+    nb, kb = Np // CHUNK_ROWS, Kp // CHUNK_K
+    # pairs index: [kb, g, p(16)] ; rows: [nb, r]
+    d = bp.reshape(kb, 2, 16, nb, CHUNK_ROWS)  # [kb, g, p, nb, r]
+    perm = np.array([w + 4 * b for w in range(4) for b in range(4)])  # position j -> pair
+    d = d[:, :, perm, :, :]  # [kb, g, j, nb, r]
+    d = d.transpose(3, 0, 1, 4, 2).reshape(nb, kb, CHUNK_DATA)  # [nb, kb, g, r, j]
+    s = bs.reshape(kb, 2, nb, CHUNK_ROWS).transpose(2, 0, 1, 3).reshape(nb, kb, 2 * CHUNK_ROWS)
+    return np.ascontiguousarray(np.concatenate([d, s], axis=2))
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns with round-to-nearest-even (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)

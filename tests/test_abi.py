@@ -1,0 +1,65 @@
+"""CPU tests of the C ABI: the library loads, exports every declared symbol, and the
+non-compute entry points behave (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "mxfp4_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(mxfp4_[a-z_0-9]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    from mxfp4_b200 import _lib
+
+    return _lib
+
+
+def test_exports_every_declared_symbol(L):
+    lib = L.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 13
+    assert sorted(L.EXPORTED) == syms
+    for s in syms:
+        assert hasattr(lib, s), s
+
+
+def test_abi_version_and_queries(L):
+    lib = L.lib()
+    assert lib.mxfp4_abi_version() == 1
+    # 3072 x 3072: 24 x 48 chunks of 4352 bytes = packed + scales exactly
+    assert lib.mxfp4_prepacked_bytes(3072, 3072) == 3072 * 3072 // 2 + 3072 * 3072 // 32
+    assert lib.mxfp4_prepacked_bytes(200, 96) == 2 * 2 * 4352
+    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_PREPACKED) == 0
+    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_REF) == lib.mxfp4_prepacked_bytes(3072, 3072)
+    assert lib.mxfp4_select_path(1, 8192, 8192) == L.PATH_GEMV
+    assert lib.mxfp4_select_path(16, 8192, 8192) == L.PATH_GEMV
+    assert lib.mxfp4_select_path(4608, 9216, 3072) == L.PATH_TC
+    assert lib.mxfp4_shape_supported(L.PATH_TC, 4608, 9216, 3072) == 1
+    assert lib.mxfp4_shape_supported(L.PATH_GEMV, 17, 9216, 3072) == 0
+    assert lib.mxfp4_shape_supported(L.PATH_TC, 128, 3072, 100) == 0  # K % 32
+    assert lib.mxfp4_shape_supported(L.PATH_TC, 128, 3071, 128) == 0  # N % 8
+
+
+def test_invalid_arguments_rejected_before_any_launch(L):
+    lib = L.lib()
+    P = ctypes.c_void_p
+    # null pointers / bad enums come back as MXFP4_ERR_INVALID_ARGUMENT without touching CUDA
+    assert lib.mxfp4_gemm(None, None, None, None, 0, 8, 8, 32, 0, 0, None, 0, None) == 1000
+    assert lib.mxfp4_gemm(P(16), P(16), P(16), P(16), 7, 8, 8, 32, 0, 0, None, 0, None) == 1000
+    assert lib.mxfp4_gemm(P(16), P(16), P(16), P(16), 0, 8, 8, 32, 9, 0, None, 0, None) == 1000
+    assert lib.mxfp4_gemm(P(16), P(16), P(16), P(16), 0, 8, 8, 33, 0, 0, None, 0, None) == 1001
+    assert lib.mxfp4_gemm(P(17), P(16), P(16), P(16), 0, 8, 8, 32, 3, 0, None, 0, None) == 1002
+    assert lib.mxfp4_quantize(None, 32, 32, 0, 0, None, None, None) == 1000
+    assert lib.mxfp4_quantize(P(16), 33, 32, 0, 0, P(16), P(16), None) == 1001
+    assert lib.mxfp4_prepack(P(16), P(16), 100, 64, 2, P(16), None) == 1001  # G needs N % 128
+    assert "workspace" in L.error_string(1003)

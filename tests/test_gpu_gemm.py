@@ -1,0 +1,137 @@
+"""GPU parity of the GEMM paths against the oracle (max|err|/max|ref| <= 1e-2, plus the
+reference's own validate.py criterion np.allclose(atol=1e-2, rtol=2e-2) for fp32 C)."""
+
+import numpy as np
+import pytest
+import torch
+
+import mxfp4_ref as o
+from _util import make_case, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2  # max|err| / max|ref|
+
+
+@pytest.fixture(scope="module")
+def mx():
+    import mxfp4_b200
+
+    return mxfp4_b200
+
+
+def _run(mx, A, Bp, Bs, path, out_dtype):
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).to(torch.bfloat16).cuda()
+    C = mx.gemm(At, w, out_dtype=out_dtype, path=path)
+    torch.cuda.synchronize()
+    assert mx.device_error() == 0
+    return C.float().cpu().numpy()
+
+
+SHAPES_TC = [
+    (256, 256, 128),  # validate.py defaults
+    (512, 512, 256),
+    (1024, 1024, 256),
+    (300, 200, 96),  # ragged M, N % 128 != 0, K % 64 != 0
+    (128, 3072, 3072),  # config 0
+    (17, 384, 512),
+    (513, 1152, 640),
+]
+
+
+@pytest.mark.parametrize("path", ["tc", "tc_smem"])
+@pytest.mark.parametrize("M,N,K", SHAPES_TC)
+def test_tc_paths_match_oracle(mx, path, M, N, K):
+    A, Bp, Bs = make_case(M, N, K, seed=M * 7 + N + K)
+    ref = o.ref_gemm(A, Bp, Bs)
+    C32 = _run(mx, A, Bp, Bs, path, torch.float32)
+    assert rel_err(C32, ref) <= TOL
+    assert np.allclose(C32, ref, atol=1e-2, rtol=2e-2)
+    C16 = _run(mx, A, Bp, Bs, path, torch.bfloat16)
+    assert rel_err(C16, ref) <= TOL
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 9, 16])
+@pytest.mark.parametrize("N,K", [(1024, 2048), (200, 96), (384, 8192)])
+def test_gemv_path_matches_oracle(mx, M, N, K):
+    A, Bp, Bs = make_case(M, N, K, seed=M + N + K)
+    ref = o.ref_gemm(A, Bp, Bs)
+    C32 = _run(mx, A, Bp, Bs, "gemv", torch.float32)
+    assert rel_err(C32, ref) <= TOL
+    assert np.allclose(C32, ref, atol=1e-2, rtol=2e-2)
+    assert rel_err(_run(mx, A, Bp, Bs, "gemv", torch.bfloat16), ref) <= TOL
+
+
+def test_gemv_extreme_activation_range(mx):
+    """Rows whose magnitudes sit far outside f16 range (the per-row power-of-two staging)."""
+    M, N, K = 4, 256, 512
+    A, Bp, Bs = make_case(M, N, K, seed=3)
+    A = A.copy()
+    A[0] *= np.float32(2.0**100)
+    A[1] *= np.float32(2.0**-100)
+    A[2, :] = 0.0
+    ref = o.ref_gemm(A, Bp, Bs)
+    got = _run(mx, A, Bp, Bs, "gemv", torch.float32)
+    for m in range(M):
+        scale = max(np.max(np.abs(ref[m])), 1e-38)
+        assert np.max(np.abs(got[m] - ref[m])) / scale <= TOL
+    assert (got[2] == 0).all()
+
+
+def test_edge_scales_through_gemm(mx):
+    """Scale bytes 0 (subnormal 2^-127), 1, 2 and 200 go through the tensor-core dequant."""
+    M, N, K = 256, 128, 128
+    rng = np.random.default_rng(9)
+    A = rng.standard_normal((M, K), dtype=np.float32).astype(np.float32)
+    A = o.bf16_bits_to_f32(o.f32_to_bf16_bits(A))
+    Bp = rng.integers(0, 256, size=(K // 2, N), dtype=np.uint8)
+    Bs = rng.choice(np.array([0, 1, 2, 200], np.uint8), size=(K // 32, N))
+    ref = o.ref_gemm(A, Bp, Bs)
+    for path in ("tc", "gemv" if M <= 16 else "tc_smem"):
+        got = _run(mx, A, Bp, Bs, path, torch.float32)
+        assert rel_err(got, ref) <= TOL, path
+
+
+def test_output_bounds_canary(mx):
+    """The kernels write exactly C[M, N]: NaN-poisoned C fully overwritten, guard band intact."""
+    M, N, K = 300, 200, 128
+    A, Bp, Bs = make_case(M, N, K, seed=1)
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).to(torch.bfloat16).cuda()
+    for path, MM in (("tc", M), ("tc_smem", M), ("gemv", 16)):
+        buf = torch.full((MM * N + 4096,), float("nan"), dtype=torch.float32, device="cuda")
+        buf[MM * N:] = 7.0
+        C = buf[: MM * N].view(MM, N)
+        mx.gemm(At[:MM].contiguous(), w, path=path, C=C)
+        torch.cuda.synchronize()
+        assert not torch.isnan(C).any(), path
+        assert (buf[MM * N:] == 7.0).all(), path
+
+
+@pytest.mark.parametrize("M,N,K", [(4608, 9216, 3072), (4608, 3072, 12288)])
+def test_full_size_against_library_gemm(mx, M, N, K):
+    """Flux-sized property check: fused kernel vs exact dequant + fp32 cuBLAS on the GPU."""
+    gen = torch.Generator(device="cuda").manual_seed(M + N)
+    A = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
+    W = torch.randn((K, N), generator=gen, device="cuda") * 0.02
+    Bp, Bs = mx.quantize_mxfp4(W, axis=0, rule="ocp")
+    w = mx.prepack_b200(Bp, Bs)
+    ref = A.float() @ mx.dequantize_mxfp4(Bp, Bs, axis=0)
+    for path in ("tc", "tc_smem"):
+        C = mx.gemm(A, w, path=path).float()
+        err = ((C - ref).abs().max() / ref.abs().max()).item()
+        assert err <= TOL, (path, err)
+    assert mx.device_error() == 0
+
+
+def test_decode_full_size_against_library_gemm(mx):
+    M, N, K = 16, 57344, 8192
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randn((M, K), generator=gen, device="cuda").to(torch.bfloat16)
+    W = torch.randn((K, N), generator=gen, device="cuda") * 0.02
+    Bp, Bs = mx.quantize_mxfp4(W, axis=0, rule="ocp")
+    w = mx.prepack_b200(Bp, Bs)
+    ref = A.float() @ mx.dequantize_mxfp4(Bp, Bs, axis=0)
+    C = mx.gemm(A, w, path="gemv").float()
+    assert ((C - ref).abs().max() / ref.abs().max()).item() <= TOL
