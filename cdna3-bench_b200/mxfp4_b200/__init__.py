@@ -19,6 +19,8 @@ _OPS = (
     "dequantize_prepacked",
     "MXFP4Weight",
     "gemm",
+    "gemm_packed",
+    "workspace_bytes",
     "gemm_auto",
     "gemm_a",
     "gemm_b",

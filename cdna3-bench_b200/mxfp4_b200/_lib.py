@@ -11,7 +11,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libmxfp4_b200.so")
+# MXFP4_B200_LIB may point at another build of the same library (e.g. a profiling build)
+LIB_PATH = os.environ.get("MXFP4_B200_LIB") or os.path.join(_HERE, "libmxfp4_b200.so")
 
 LAYOUT_REF, LAYOUT_NK, LAYOUT_G, LAYOUT_PREPACKED = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16 = 0, 1

@@ -243,6 +243,34 @@ def _gemm_layout(A, B, Bs, C, layout: int, N: int, K: int, path: int, name: str)
     return C
 
 
+def workspace_bytes(M: int, N: int, K: int, layout: str = "ref") -> int:
+    return int(_lib.lib().mxfp4_gemm_workspace_bytes(M, N, K, _LAYOUTS[layout]))
+
+
+def gemm_packed(A, B_packed, B_scales, out_dtype=torch.bfloat16, layout: str = "ref", C=None,
+                workspace=None, path: str = "auto"):
+    """C = A @ dequant(B) for weights in the reference ([K/2,N]) or row-major ([N,K/2]) layout,
+    bf16 or fp32 output.  The weights are re-laid into ``workspace`` (allocated when not given,
+    ``workspace_bytes`` long) inside the same call, so this is the one-call drop-in path."""
+    _check_A(A)
+    M, K = A.shape
+    N = B_packed.shape[1] if layout == "ref" else B_packed.shape[0]
+    if C is None:
+        C = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    _check(C.is_cuda and C.dtype in _ODT and tuple(C.shape) == (M, N) and C.is_contiguous(), "C shape/contig")
+    need = workspace_bytes(M, N, K, layout)
+    if workspace is None:
+        workspace = torch.empty(max(1, need), dtype=torch.uint8, device=A.device)
+    _check(workspace.numel() >= need, "workspace too small")
+    _lib.check(
+        _lib.lib().mxfp4_gemm(_ptr(A), _ptr(B_packed), _ptr(B_scales), _ptr(C), _ODT[C.dtype], M, N, K,
+                              _LAYOUTS[layout], _lib.PATH_NAMES[path], _ptr(workspace), workspace.numel(),
+                              _stream()),
+        "mxfp4_gemm",
+    )
+    return C
+
+
 def _check_ref_inputs(A, B_packed, B_scales):
     for t in (A, B_packed, B_scales):
         _check(isinstance(t, torch.Tensor) and t.is_cuda, "all tensors must be on GPU")
