@@ -237,6 +237,8 @@ const char* mxfp4_error_string(int code) {
     case MXFP4_ERR_WORKSPACE: return "mxfp4: workspace missing or too small";
     case MXFP4_ERR_DRIVER: return "mxfp4: tensor-map encoder unavailable or rejected the tensor";
     case MXFP4_ERR_DEVICE: return "mxfp4: current device is not an sm_100 GPU";
+    case MXFP4_ERR_NOALLOC_LIMIT:
+      return "mxfp4: weights need more than the 32 MiB buffer of mxfp4_gemm_noalloc (use mxfp4_gemm)";
     default: return cudaGetErrorString(static_cast<cudaError_t>(code));
   }
 }
@@ -379,3 +381,48 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of mxfp4_gemm for callers that may not allocate device memory.
+// The library carries its own buffer for the re-laid weights.  Host code only knows the
+// array by its host-side symbol, so the device address is looked up once per device (with
+// that device current) and cached; the kernels then get that address like any workspace.
+// The prepack writes every byte of the region the GEMM reads, so nothing in the buffer has
+// to be cleared between calls; concurrent calls share it and must not overlap on the GPU.
+namespace mxb {
+namespace {
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MXFP4_NOALLOC_SCRATCH_BYTES];
+void* g_noalloc_ptr[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ret(e);
+  if (dev < 0 || dev >= kMaxDevices) return MXFP4_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return ret(e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+}  // namespace
+}  // namespace mxb
+
+extern "C" int mxfp4_gemm_noalloc(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
+                                  int M, int N, int K, int layout, int path, void* stream) {
+  if (layout != MXFP4_LAYOUT_REF && layout != MXFP4_LAYOUT_NK && layout != MXFP4_LAYOUT_G)
+    return MXFP4_ERR_INVALID_ARGUMENT;  // prepacked weights need no buffer: call mxfp4_gemm
+  if (N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  const size_t need = mxb::prepacked_bytes(N, K);
+  if (need > MXFP4_NOALLOC_SCRATCH_BYTES) return MXFP4_ERR_NOALLOC_LIMIT;
+  void* scratch = nullptr;
+  const int rc = mxb::noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return mxfp4_gemm(A, B, B_scales, C, c_dtype, M, N, K, layout, path, scratch, MXFP4_NOALLOC_SCRATCH_BYTES,
+                    stream);
+}

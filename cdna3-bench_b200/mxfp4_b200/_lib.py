@@ -36,6 +36,7 @@ EXPORTED = (
     "mxfp4_shape_supported",
     "mxfp4_gemm_workspace_bytes",
     "mxfp4_gemm",
+    "mxfp4_gemm_noalloc",
 )
 
 
@@ -79,6 +80,7 @@ def _declare(lib):
         "mxfp4_shape_supported": (_I, [_I, _I, _I, _I]),
         "mxfp4_gemm_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
         "mxfp4_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+        "mxfp4_gemm_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -59,6 +59,7 @@ enum mxfp4_quant_rule {
 #define MXFP4_ERR_WORKSPACE 1003 /* workspace missing or smaller than required */
 #define MXFP4_ERR_DRIVER 1004 /* driver entry point (tensor-map encoder) unavailable */
 #define MXFP4_ERR_DEVICE 1005 /* current device is not an sm_100 part */
+#define MXFP4_ERR_NOALLOC_LIMIT 1006 /* weights too large for the fixed buffer of mxfp4_gemm_noalloc */
 
 typedef struct mxfp4_device_info {
   char name[256];
@@ -129,6 +130,24 @@ size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout);
 int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
                int M, int N, int K, int layout, int path, void* workspace, size_t workspace_bytes,
                void* stream);
+
+/* Fixed size of the device buffer mxfp4_gemm_noalloc uses in place of a workspace. */
+#define MXFP4_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* No counterpart in the reference.  Same as mxfp4_gemm for weights in the REF, NK or G layout,
+ * but for callers that cannot allocate device memory -- code that must not call cudaMalloc
+ * (a custom or pool allocator owns all device memory, an allocation would synchronise the
+ * device mid-pipeline, or the caller is a plugin with no allocator handle) and so cannot
+ * hand over the workspace mxfp4_gemm wants.  The re-laid weights go into a buffer that is
+ * part of the library itself: a fixed MXFP4_NOALLOC_SCRATCH_BYTES (32 MiB) device array
+ * that every GPU which loads the library holds until the process exits.  Weights needing
+ * more than that (mxfp4_prepacked_bytes(N, K) > 32 MiB, e.g. beyond about N*K = 63M
+ * elements) are rejected with MXFP4_ERR_NOALLOC_LIMIT.  The first call on a device looks up
+ * the buffer's device address for that device; make that first call before any stream
+ * capture.  All calls share the one buffer, so calls that may overlap on the GPU (different
+ * streams, or several host threads) race on it and give wrong results; serialise them. */
+int mxfp4_gemm_noalloc(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
+                       int M, int N, int K, int layout, int path, void* stream);
 
 #ifdef __cplusplus
 }
