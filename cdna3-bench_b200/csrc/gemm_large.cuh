@@ -13,21 +13,34 @@
 //       kTS = true : into tensor memory with tcgen05.st (the MMA reads A from TMEM, which
 //                    keeps the dequantised tile off the shared-memory bandwidth), or
 //       kTS = false: into a 128B-swizzled K-major smem tile (classic SS MMA).
-//   * Accumulator: 128 lanes x 256 f32 columns of TMEM; the epilogue reads it with
-//     tcgen05.ld, converts to the output type, stages 32-row slabs in smem and writes
-//     them with TMA tensor stores.
+//   * Accumulator: 128 lanes x 256 f32 columns of TMEM.  Eight epilogue warps (two per TMEM
+//     lane quarter, one per 128-column half) read their columns into registers (packed to
+//     bf16) and hand the accumulator back to the MMA issuer BEFORE storing, so the next
+//     tile's MMAs overlap the stores; each warp then writes 32 x 32 slabs through its own
+//     smem staging buffer with TMA tensor stores.
 //   * Persistent CTAs (one per SM) walk the tile list in a grouped raster order.
 //
-// Warp roles (448 threads): 0 = TMA producer, 1 = MMA issuer (+TMEM owner),
-// 2..5 = epilogue (one per TMEM lane quarter), 6..13 = dequant (two per lane quarter,
-// one per 32-element half of the stage).
+// Warp roles (576 threads): 0 = TMA producer, 1 = MMA issuer (+TMEM owner),
+// 2..9 = epilogue, 10..17 = dequant (two per TMEM lane quarter, one per 32-element half of
+// the stage).  A warp may touch TMEM lanes 32*(warp%4) .. +31 only.
 #pragma once
 
 #include "common.cuh"
 
+// Profiling switch, 0 in every product build.  -DMXFP4_TC_DIAG=<bit mask> removes pipeline
+// stages so the remaining ones can be timed in isolation (results are then wrong):
+//   1: dequant warps skip the table lookup (zeros go to TMEM),  2: ... skip the TMEM store,
+//   4: the MMA issuer commits without issuing MMAs,  8: the epilogue skips staging and stores.
+#ifndef MXFP4_TC_DIAG
+#define MXFP4_TC_DIAG 0
+#endif
+
 namespace mxb {
 
-constexpr int kTcThreads = 448;
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcFirstEpiWarp = 2;
+constexpr int kTcFirstDqWarp = kTcFirstEpiWarp + kTcEpiWarps;
+constexpr int kTcThreads = 32 * (kTcFirstDqWarp + 8);  // 576
 constexpr int kTcTileAct = 256;  // activation rows per tile (UMMA N)
 constexpr int kTcTileW = 128;    // weight rows per tile (UMMA M)
 constexpr int kTcBK = 64;
@@ -40,10 +53,10 @@ struct TcCfg {
   static constexpr int kStages = kTS ? 5 : 3;
   static constexpr int kActBytes = kTcTileAct * kTcBK * 2;          // 32 KiB
   static constexpr int kATileBytes = kTS ? 0 : kTcTileW * kTcBK * 2;  // 16 KiB (SS only)
-  static constexpr int kOutSlabBytes = 32 * kTcTileW * static_cast<int>(sizeof(OutT));
+  static constexpr int kSlabBytes = 32 * 32 * static_cast<int>(sizeof(OutT));  // 32 m x 32 n
   static constexpr int kOffA = kStages * kActBytes;
   static constexpr int kOffOut = kOffA + kStages * kATileBytes;
-  static constexpr int kOffW = kOffOut + 2 * kOutSlabBytes;
+  static constexpr int kOffW = kOffOut + kTcEpiWarps * kSlabBytes;
   static constexpr int kOffBar = kOffW + kStages * kChunkBytes;
   static constexpr int kNumBars = 3 * kStages + 2;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -60,15 +73,6 @@ __device__ __forceinline__ void tc_tile_coords(int t, int m_blocks, int n_blocks
   const int local = t - grp * per_group;
   mb = first + local % gm;
   nb = local / gm;
-}
-
-template <typename OutT>
-__device__ __forceinline__ OutT f32_bits_to(uint32_t v);
-template <>
-__device__ __forceinline__ float f32_bits_to<float>(uint32_t v) { return __uint_as_float(v); }
-template <>
-__device__ __forceinline__ __nv_bfloat16 f32_bits_to<__nv_bfloat16>(uint32_t v) {
-  return __float2bfloat16_rn(__uint_as_float(v));
 }
 
 template <bool kTS, typename OutT>
@@ -98,7 +102,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 4);
+    mbar_init(acc_empty, kTcEpiWarps);
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_act);
@@ -168,6 +172,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t bdesc = umma_desc_sw128(smem_u32(smem + s * Cfg::kActBytes));
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
+            if (MXFP4_TC_DIAG & 4) break;
             const uint32_t acc = (kb | i) != 0;
             if constexpr (kTS) {
               mma_ts(tmem + kTmemAccCol, tmem + kTmemARingCol + s * 32 + i * 8, bdesc + 2 * i, idesc, acc);
@@ -192,50 +197,91 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_wait_drain(acc_full, aph);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < kTcFirstDqWarp) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const bool leader = threadIdx.x == 64;
+    const int q = warp & 3;   // TMEM lane quarter = 32 output columns
+    const int ew = warp - kTcFirstEpiWarp;
+    const int hh = ew >> 2;   // 128-column half of the accumulator
+    uint8_t* stage_ptr = smem + Cfg::kOffOut + ew * Cfg::kSlabBytes;
+    const uint32_t stage = smem_u32(stage_ptr);
     uint32_t aph = 0;
-    int slab = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int mb, nb;
       tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
       if (!warp_wait(acc_full, aph, kErrWaitAccFull, abort_flag)) break;
       tc_fence_after();
-      const int m0 = mb * kTcTileAct;
-      const int live = min(kTcTileAct / 32, ceil_div(M - m0, 32));
-      for (int c = 0; c < live; ++c) {
-        const int buf = slab & 1;
-        ++slab;
-        if (leader) bulk_wait_read<1>();
-        named_bar_sync(1, 128);
-        uint32_t v[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemAccCol + c * 32, v);
-        tmem_wait_ld();
-        if (c == live - 1) {  // whole accumulator read: hand TMEM back to the MMA issuer
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty);
-        }
-        OutT* st = reinterpret_cast<OutT*>(smem + Cfg::kOffOut + buf * Cfg::kOutSlabBytes);
+      const int m0 = mb * kTcTileAct + 128 * hh;  // activation rows m0 .. m0+127 of this warp
+      const int n0 = nb * kTcTileW + 32 * q;      // output columns n0 .. n0+31 (one per lane)
+      const uint32_t tb = tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemAccCol + 128 * hh;
+      if constexpr (sizeof(OutT) == 2) {
+        uint32_t packed[64];  // bf16 pairs (m, m+1) of this lane's output column
 #pragma unroll
-        for (int j = 0; j < 32; ++j) st[j * kTcTileW + 32 * q + lane] = f32_bits_to<OutT>(v[j]);
-        fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (leader) {
-          tma_store_2d(&tm_out, st, nb * kTcTileW, m0 + c * 32);
-          bulk_commit();
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+          tmem_ld16(tb + 16 * c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            packed[8 * c + j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);  // accumulator free: the next tile's MMAs start
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // four 32-row slabs
+          const int mc = m0 + 32 * c;
+          if (!(MXFP4_TC_DIAG & 8) && mc < M) {
+            if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t pk = packed[16 * c + j];
+              sts16(stage + ((2 * j) * 32 + lane) * 2, pk & 0xFFFFu);
+              sts16(stage + ((2 * j + 1) * 32 + lane) * 2, pk >> 16);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_out, stage_ptr, n0, mc);
+              bulk_commit();
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {  // f32 output: 32-column chunks, release after the last load
+          uint32_t v[32];
+          tmem_ld32(tb + 32 * c, v);
+          tmem_wait_ld();
+          if (c == 3) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+          }
+          const int mc = m0 + 32 * c;
+          if (!(MXFP4_TC_DIAG & 8) && mc < M) {
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sts32(stage + (j * 32 + lane) * 4, v[j]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tm_out, stage_ptr, n0, mc);
+              bulk_commit();
+            }
+          }
         }
       }
       aph ^= 1;
     }
-    if (leader) bulk_wait_all();
+    if (lane == 0) bulk_wait_all();
   } else {
     // ------------------------------------------------------------ dequant
     const int q = warp & 3;
-    const int h = (warp - 6) >> 2;  // which 32-element group of the stage
-    const int r = 32 * q + lane;    // weight row inside the tile == TMEM lane
+    const int h = (warp - kTcFirstDqWarp) >> 2;  // which 32-element group of the stage
+    const int r = 32 * q + lane;                 // weight row inside the tile == TMEM lane
+    const uint32_t wbase = smem_u32(smem + Cfg::kOffW);
     int s = 0;
     uint32_t ph = 0;
     bool aborted = false;
@@ -245,21 +291,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           aborted = true;
           break;
         }
-        const uint8_t* wst = smem + Cfg::kOffW + s * kChunkBytes;
-        const uint4 d = *reinterpret_cast<const uint4*>(wst + h * (kChunkRows * 16) + r * 16);
+        const uint32_t wst = wbase + s * kChunkBytes;
         uint32_t v[16];
-        dequant_rowgroup(d, wst[kChunkData + h * kChunkRows + r], v);
-        if constexpr (kTS) {
+        if (MXFP4_TC_DIAG & 1) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0;
+        } else {
+          const uint4 d = lds128(wst + h * (kChunkRows * 16) + r * 16);
+          dequant_rowgroup(d, lds_u8(wst + kChunkData + h * kChunkRows + r), v);
+        }
+        if (MXFP4_TC_DIAG & 2) {
+        } else if constexpr (kTS) {
           tc_fence_after();
           tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemARingCol + s * 32 + h * 16, v);
           tmem_wait_st();
           tc_fence_before();
         } else {
-          uint8_t* at = smem + Cfg::kOffA + s * Cfg::kATileBytes + r * 128;
+          const uint32_t at = smem_u32(smem + Cfg::kOffA + s * Cfg::kATileBytes) + r * 128;
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(at + (((4 * h + j) ^ (r & 7)) << 4)) =
-                make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            sts128(at + (((4 * h + j) ^ (r & 7)) << 4),
+                   make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
           fence_proxy_async_smem();
         }
         __syncwarp();

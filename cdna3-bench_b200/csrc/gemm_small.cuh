@@ -31,7 +31,8 @@ struct GvCfg {
   static constexpr int kMP = 8 * NT;  // padded activation rows
   static constexpr int kOffBar = kGvRing * kChunkBytes;
   static constexpr int kOffShift = kOffBar + 2 * kGvRing * 8;
-  static constexpr int kOffRed = (kOffShift + 4 * kMP + 16 + 127) & ~127;
+  static constexpr int kOffMax = kOffShift + 4 * kMP + 16;
+  static constexpr int kOffRed = (kOffMax + 4 * kMP + 127) & ~127;
   static constexpr int kOffX = kOffRed + kChunkRows * kMP * 4;
   static constexpr int kXBytesPerKb = 2 * kMP * 64;  // two 32-groups x MP rows x 16 f16 pairs
   static int smem_bytes(int kb_per_split) { return kOffX + kb_per_split * kXBytesPerKb; }
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(kGvThreads)
   uint64_t* empty = full + kGvRing;
   int* xshift = reinterpret_cast<int*>(smem + Cfg::kOffShift);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(xshift + MP);
+  float* xmax = reinterpret_cast<float*>(smem + Cfg::kOffMax);
   float* red = reinterpret_cast<float*>(smem + Cfg::kOffRed);
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Cfg::kOffX);
 
@@ -99,6 +101,7 @@ __global__ void __launch_bounds__(kGvThreads)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (threadIdx.x < MP) xmax[threadIdx.x] = 0.0f;
   __syncthreads();
 
   if (warp == 8) {
@@ -126,12 +129,19 @@ __global__ void __launch_bounds__(kGvThreads)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ stage activations (f16)
+    // All 256 compute threads split the staged K range.  Pass 1: per-row max |x| (warp
+    // reduce + shared atomicMax on the float bits, valid for non-negative floats).  Pass 2:
+    // scale by 2**shift and convert to f16 pairs.  Layout: block (grp, m, t) of 16 bytes holds
+    // pairs t, t+4, t+8, t+12 of group grp for row m, stored at block position
+    // (grp*MP + m)*4 + (t ^ (grp & 3)) so that the pass-2 word stores spread over the banks.
     const int k_lo = kb0 * 64;
-    const int k_end = (kb0 + nkb) * 64;  // staged range, zero-padded beyond K
-    for (int m = warp; m < MP; m += 8) {
+    const int nvec = nkb * 8;  // 16-byte vectors (8 bf16) per row in the staged range
+    const int tid = threadIdx.x;
+    for (int m = 0; m < M; ++m) {
       float amax = 0.0f;
-      if (m < M) {
-        for (int k = k_lo + lane * 8; k < min(K, k_end); k += 256) {
+      for (int v = tid; v < nvec; v += 256) {
+        const int k = k_lo + v * 8;
+        if (k < K) {
           const uint4 raw = *reinterpret_cast<const uint4*>(A + static_cast<size_t>(m) * K + k);
           const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -143,26 +153,34 @@ __global__ void __launch_bounds__(kGvThreads)
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0 && amax > 0.0f) atomicMax(reinterpret_cast<unsigned*>(xmax) + m, __float_as_uint(amax));
+    }
+    named_bar_sync(1, 256);
+    if (tid < MP) {
+      const float amax = __uint_as_float(reinterpret_cast<unsigned*>(xmax)[tid]);
       int shift = 0;
       if (amax > 0.0f && amax <= 3.0e38f) {
         int E;
         frexpf(amax, &E);
-        shift = 15 - E;  // row max lands in [2^14, 2^15)
+        shift = 15 - E;  // the row max lands in [2^14, 2^15)
       }
-      if (lane == 0) xshift[m] = shift;
-      for (int k = k_lo + lane * 8; k < k_end; k += 256) {
-        uint4 raw = make_uint4(0, 0, 0, 0);
-        if (m < M && k < K) raw = *reinterpret_cast<const uint4*>(A + static_cast<size_t>(m) * K + k);
-        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-        const int pair0 = (k - k_lo) >> 1;  // multiple of 4
-        const int grp = pair0 >> 4;
-        const int slot = (pair0 & 15) >> 2;
+      xshift[tid] = shift;
+    }
+    named_bar_sync(1, 256);
+    for (int e = tid; e < MP * nvec; e += 256) {
+      const int m = e / nvec, v = e - m * nvec;
+      const int k = k_lo + v * 8;
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (m < M && k < K) raw = *reinterpret_cast<const uint4*>(A + static_cast<size_t>(m) * K + k);
+      const int shift = xshift[m];
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      const int grp = v >> 2, slot = v & 3;  // vector v = pairs 4*slot .. 4*slot+3 of group grp
+      const uint32_t blk = smem_u32(xs + (grp * MP + m) * 16 + slot);
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float lo = ldexpf(__uint_as_float(w[t] << 16), shift);
-          const float hi = ldexpf(__uint_as_float(w[t] & 0xFFFF0000u), shift);
-          xs[((grp * MP + m) * 4 + t) * 4 + slot] = f16x2_from(lo, hi);
-        }
+      for (int t = 0; t < 4; ++t) {
+        const float lo = ldexpf(__uint_as_float(w[t] << 16), shift);
+        const float hi = ldexpf(__uint_as_float(w[t] & 0xFFFF0000u), shift);
+        sts32(blk + (t ^ (grp & 3)) * 16, f16x2_from(lo, hi));
       }
     }
     named_bar_sync(1, 256);
@@ -173,22 +191,25 @@ __global__ void __launch_bounds__(kGvThreads)
     float acc[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    const uint32_t ring_a = smem_u32(ring);
+    const uint32_t xs_a = smem_u32(xs);
     for (int i = 0; i < nkb; ++i) {
       const int s = i % kGvRing;
       if (!warp_wait(&full[s], (i / kGvRing) & 1, kErrWaitFull, abort_flag)) break;
-      const uint8_t* ch = ring + s * kChunkBytes;
+      const uint32_t ch = ring_a + s * kChunkBytes;
 #pragma unroll
       for (int G = 0; G < 2; ++G) {
-        const uint32_t wl = *reinterpret_cast<const uint32_t*>(ch + G * 2048 + row * 16 + 4 * t);
-        const uint32_t wh = *reinterpret_cast<const uint32_t*>(ch + G * 2048 + (row + 8) * 16 + 4 * t);
-        const float sl = e8m0_to_f32(ch[kChunkData + G * kChunkRows + row]);
-        const float sh = e8m0_to_f32(ch[kChunkData + G * kChunkRows + row + 8]);
+        const uint32_t wl = lds32(ch + G * 2048 + row * 16 + 4 * t);
+        const uint32_t wh = lds32(ch + G * 2048 + (row + 8) * 16 + 4 * t);
+        const float sl = e8m0_to_f32(lds_u8(ch + kChunkData + G * kChunkRows + row));
+        const float sh = e8m0_to_f32(lds_u8(ch + kChunkData + G * kChunkRows + row + 8));
         uint32_t fl[4], fh[4];
         e2m1x8_to_f16x2(wl, fl);
         e2m1x8_to_f16x2(wh, fh);
+        const int xg = 2 * i + G;
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
-          const uint4 xb = *reinterpret_cast<const uint4*>(xs + (((2 * i + G) * MP + 8 * j + g) * 4 + t) * 4);
+          const uint4 xb = lds128(xs_a + (((xg * MP + 8 * j + g) * 4 + (t ^ (xg & 3))) * 4) * 4);
           float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
           mma_f16_16816(d, fl[0], fh[0], fl[1], fh[1], xb.x, xb.y);
           mma_f16_16816(d, fl[2], fh[2], fl[3], fh[3], xb.z, xb.w);

@@ -102,7 +102,7 @@ int launch_tc(const void* A, const uint8_t* wpack, void* C, int M, int N, int K,
   if (rc) return rc;
   rc = encode_2d(&tm_out,
                  sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                 static_cast<int>(sizeof(OutT)), C, N, M, kTcTileW, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+                 static_cast<int>(sizeof(OutT)), C, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
   const int m_blocks = ceil_div(M, kTcTileAct);
   const int n_blocks = n_blocks_of(N);
@@ -125,8 +125,9 @@ GvPlan plan_gemv(int M, int N, int K, int sm_count) {
   const int x_per_kb = 2 * (8 * p.nt) * 64;
   const int fixed = p.nt == 1 ? GvCfg<1>::kOffX : GvCfg<2>::kOffX;
   p.ks = 1;
-  // enough CTAs to cover every SM twice, and the staged activations within ~96 KiB
-  while (p.ks < 8 && (nb * p.ks < 2 * sm_count || ceil_div(kb, p.ks) * x_per_kb > 96 * 1024)) p.ks *= 2;
+  // K-split across the cluster until there are ~3 CTAs per SM and each CTA's K range is at
+  // most 2048 (32 chunks), so the staged activations stay small and 2-3 CTAs fit on an SM
+  while (p.ks < 8 && (nb * p.ks < 3 * sm_count || ceil_div(kb, p.ks) > 32)) p.ks *= 2;
   p.kbps = ceil_div(kb, p.ks);
   p.smem = fixed + p.kbps * x_per_kb;
   return p;
