@@ -25,6 +25,18 @@ constexpr int kChunkK = 64;         // K elements per prepacked chunk
 constexpr int kChunkData = kChunkRows * kChunkK / 2;                     // 4096 B of nibbles
 constexpr int kChunkBytes = kChunkData + kChunkRows * (kChunkK / kGroup);  // + 256 B scales
 
+// Chunk byte layout.  Word t (bytes b = 0..3 hold k-pairs t + 4b of the group) of row r's
+// 32-group grp sits in 16-byte unit 32*(r/16) + 4*(r%8) + t, at word 2*grp + (r/8)%2: one unit
+// holds the four A-fragment words lane (g = r%8, t) of an m16n8k16 MMA needs for rows
+// 16*(r/16) .. +15 and both groups.  The scales follow the data in the same order, four to a
+// 4-byte unit 8*(r/16) + r%8.
+__host__ __device__ constexpr int chunk_word_off(int r, int grp, int t) {
+  return (32 * (r >> 4) + 4 * (r & 7) + t) * 16 + (2 * grp + ((r >> 3) & 1)) * 4;
+}
+__host__ __device__ constexpr int chunk_scale_off(int r, int grp) {
+  return kChunkData + 4 * (8 * (r >> 4) + (r & 7)) + 2 * grp + ((r >> 3) & 1);
+}
+
 // ---- device error word -------------------------------------------------------------
 // First non-zero code wins; the host reads and clears it with mxfp4_device_error().
 enum DeviceError : unsigned {

@@ -297,8 +297,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = 0;
         } else {
-          const uint4 d = lds128(wst + h * (kChunkRows * 16) + r * 16);
-          dequant_rowgroup(d, lds_u8(wst + kChunkData + h * kChunkRows + r), v);
+          const uint4 d = make_uint4(lds32(wst + chunk_word_off(r, h, 0)), lds32(wst + chunk_word_off(r, h, 1)),
+                                     lds32(wst + chunk_word_off(r, h, 2)), lds32(wst + chunk_word_off(r, h, 3)));
+          dequant_rowgroup(d, lds_u8(wst + chunk_scale_off(r, h)), v);
         }
         if (MXFP4_TC_DIAG & 2) {
         } else if constexpr (kTS) {

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -128,6 +129,11 @@ GvPlan plan_gemv(int M, int N, int K, int sm_count) {
   // K-split across the cluster until there are ~3 CTAs per SM and each CTA's K range is at
   // most 2048 (32 chunks), so the staged activations stay small and 2-3 CTAs fit on an SM
   while (p.ks < 8 && (nb * p.ks < 3 * sm_count || ceil_div(kb, p.ks) > 32)) p.ks *= 2;
+  static const int ks_override = [] {
+    const char* e = std::getenv("MXFP4_GEMV_KS");  // tuning knob: force the K-split (1, 2, 4, 8)
+    return e ? std::atoi(e) : 0;
+  }();
+  if (ks_override == 1 || ks_override == 2 || ks_override == 4 || ks_override == 8) p.ks = ks_override;
   p.kbps = ceil_div(kb, p.ks);
   p.smem = fixed + p.kbps * x_per_kb;
   return p;

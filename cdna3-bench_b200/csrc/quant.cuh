@@ -224,8 +224,9 @@ __global__ void prepack_kernel(const uint8_t* __restrict__ packed, const uint8_t
     sc = src_scale(scales, layout, kg, n, K, N);
   }
   uint8_t* c = dst + chunk * kChunkBytes;
-  *reinterpret_cast<uint4*>(c + g * (kChunkRows * 16) + r * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-  c[kChunkData + g * kChunkRows + r] = static_cast<uint8_t>(sc);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) *reinterpret_cast<uint32_t*>(c + chunk_word_off(r, g, t)) = w[t];
+  c[chunk_scale_off(r, g)] = static_cast<uint8_t>(sc);
 }
 
 // Dequantise prepacked chunks to bf16 [N, K] with the GEMM kernels' table-lookup routine
@@ -245,9 +246,12 @@ __global__ void dequant_prepacked_kernel(const uint8_t* __restrict__ wpack, int 
   const int k0 = (kb * 2 + g) * kGroup;
   if (n >= N || k0 >= K) return;
   const uint8_t* c = wpack + chunk * kChunkBytes;
-  const uint4 d = *reinterpret_cast<const uint4*>(c + g * (kChunkRows * 16) + r * 16);
+  const uint4 d = make_uint4(*reinterpret_cast<const uint32_t*>(c + chunk_word_off(r, g, 0)),
+                             *reinterpret_cast<const uint32_t*>(c + chunk_word_off(r, g, 1)),
+                             *reinterpret_cast<const uint32_t*>(c + chunk_word_off(r, g, 2)),
+                             *reinterpret_cast<const uint32_t*>(c + chunk_word_off(r, g, 3)));
   uint32_t o[16];
-  dequant_rowgroup(d, c[kChunkData + g * kChunkRows + r], o);
+  dequant_rowgroup(d, c[chunk_scale_off(r, g)], o);
   uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(n) * K + k0);
 #pragma unroll
   for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);

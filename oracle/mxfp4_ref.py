@@ -163,16 +163,36 @@ CHUNK_DATA = CHUNK_ROWS * CHUNK_K // 2  # 4096 bytes of nibbles
 CHUNK_BYTES = CHUNK_DATA + CHUNK_ROWS * (CHUNK_K // GROUP)  # + 256 scale bytes = 4352
 
 
+def chunk_data_offset(r, grp, t, b):
+    """Byte offset inside a 4352-byte chunk of weight row r (0..127), 32-group grp (0..1),
+    word t (0..3) and byte b (0..3) of that row-group, where byte b of word t holds the
+    nibble pair for k-pair t + 4*b of the group (low nibble = even k).
+
+    16-byte units u = 32*w + 4*g + t, with w = r // 16 and g = r % 8, each hold word t of
+    (row 16w+g, group 0), (row 16w+g+8, group 0), (row 16w+g, group 1), (row 16w+g+8, group 1):
+    exactly the A-fragment words lane (g, t) of an m16n8k16 MMA needs for rows 16w..16w+15,
+    so a decode kernel fetches them with one 16-byte load per lane.
+    """
+    r = np.asarray(r)
+    unit = 32 * (r >> 4) + 4 * (r & 7) + t
+    word = 2 * grp + ((r >> 3) & 1)
+    return unit * 16 + word * 4 + b
+
+
+def chunk_scale_offset(r, grp):
+    """Byte offset of the E8M0 scale of row r, group grp: 4-byte units 8*w + g after the data
+    hold the scales of (row 16w+g, group 0), (16w+g+8, 0), (16w+g, 1), (16w+g+8, 1)."""
+    r = np.asarray(r)
+    return CHUNK_DATA + 4 * (8 * (r >> 4) + (r & 7)) + 2 * grp + ((r >> 3) & 1)
+
+
 def b200_prepack(B_packed, B_scales):
     """Host restatement of the B200 prepacked weight layout (the GPU prepack's oracle).
 
-    Input: reference layout B_packed [K/2, N], B_scales [K/32, N].  N is padded to
-    a multiple of 128 and K to a multiple of 64 with zero nibbles and scale 127.
-    Output: uint8 [N_pad/128, K_pad/64, 4352] where each 4352-byte chunk is
-      data  [g in 0..1][r in 0..127][16 bytes]   (g = 32-element group of the chunk)
-      scale [g in 0..1][r in 0..127]
-    and inside a row-group the 16 bytes are ordered so that 4-byte word w holds
-    the k-pairs {w, w+4, w+8, w+12} (byte b of word w = k-pair w + 4*b).
+    Input: reference layout B_packed [K/2, N], B_scales [K/32, N].  N is padded to a multiple
+    of 128 and K to a multiple of 64 with zero nibbles and scale 127.  Output: uint8
+    [N_pad/128, K_pad/64, 4352]; chunk (nb, kb) holds rows nb*128 .. +127 and k in
+    kb*64 .. +63 placed by chunk_data_offset / chunk_scale_offset.
     """
     B_packed = np.asarray(B_packed, dtype=np.uint8)
     B_scales = np.asarray(B_scales, dtype=np.uint8)
@@ -185,13 +205,16 @@ def b200_prepack(B_packed, B_scales):
     bs = np.full((Kp // GROUP, Np), 127, dtype=np.uint8)
     bs[: K // GROUP, :N] = B_scales
     nb, kb = Np // CHUNK_ROWS, Kp // CHUNK_K
-    # pairs index: [kb, g, p(16)] ; rows: [nb, r]
-    d = bp.reshape(kb, 2, 16, nb, CHUNK_ROWS)  # [kb, g, p, nb, r]
-    perm = np.array([w + 4 * b for w in range(4) for b in range(4)])  # position j -> pair
-    d = d[:, :, perm, :, :]  # [kb, g, j, nb, r]
-    d = d.transpose(3, 0, 1, 4, 2).reshape(nb, kb, CHUNK_DATA)  # [nb, kb, g, r, j]
-    s = bs.reshape(kb, 2, nb, CHUNK_ROWS).transpose(2, 0, 1, 3).reshape(nb, kb, 2 * CHUNK_ROWS)
-    return np.ascontiguousarray(np.concatenate([d, s], axis=2))
+    d = bp.reshape(kb, 2, 16, nb, CHUNK_ROWS).transpose(3, 0, 4, 1, 2)  # [nb, kb, r, grp, pair]
+    s = bs.reshape(kb, 2, nb, CHUNK_ROWS).transpose(2, 0, 3, 1)  # [nb, kb, r, grp]
+    r, g, p = np.meshgrid(np.arange(CHUNK_ROWS), np.arange(2), np.arange(16), indexing="ij")
+    doff = chunk_data_offset(r, g, p % 4, p // 4)  # pair p = t + 4*b
+    r2, g2 = np.meshgrid(np.arange(CHUNK_ROWS), np.arange(2), indexing="ij")
+    soff = chunk_scale_offset(r2, g2)
+    out = np.empty((nb, kb, CHUNK_BYTES), dtype=np.uint8)
+    out[:, :, doff.reshape(-1)] = d.reshape(nb, kb, -1)
+    out[:, :, soff.reshape(-1)] = s.reshape(nb, kb, -1)
+    return out
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:

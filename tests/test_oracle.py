@@ -116,14 +116,22 @@ def test_b200_prepack_layout_roundtrip():
     P = o.b200_prepack(Bp, Bs)
     nb, kb = -(-N // 128), -(-K // 64)
     assert P.shape == (nb, kb, o.CHUNK_BYTES)
-    for n in (0, 5, 127, 128, 199):
+    # the offsets are a bijection onto the chunk
+    r, g, p = np.meshgrid(np.arange(128), np.arange(2), np.arange(16), indexing="ij")
+    offs = np.concatenate([o.chunk_data_offset(r, g, p % 4, p // 4).ravel(),
+                           o.chunk_scale_offset(r[:, :, 0], g[:, :, 0]).ravel()])
+    assert sorted(offs.tolist()) == list(range(o.CHUNK_BYTES))
+    for n in (0, 5, 8, 15, 16, 127, 128, 199):
         for kp in (0, 3, 17, 31, 32, 79):
             c = P[n // 128, kp // 32]
             g, p = (kp % 32) // 16, kp % 16
-            w, b = p % 4, p // 4
-            assert c[g * 2048 + (n % 128) * 16 + 4 * w + b] == Bp[kp, n]
+            assert c[o.chunk_data_offset(n % 128, g, p % 4, p // 4)] == Bp[kp, n]
         for kg in range(K // 32):
-            assert P[n // 128, kg // 2, 4096 + (kg % 2) * 128 + n % 128] == Bs[kg, n]
+            assert P[n // 128, kg // 2, o.chunk_scale_offset(n % 128, kg % 2)] == Bs[kg, n]
     # padding: rows beyond N and groups beyond K are zero nibbles with scale 127
-    assert (P[1, :, 4096 + 200 - 128 : 4096 + 128] == 127).all()
-    assert (P[:, 2, 4096 + 128 :] == 127).all()  # k group 5 (k >= 160) of chunk kb=2
+    for r_ in range(200 - 128, 128):
+        for g_ in range(2):
+            assert (P[1, :, o.chunk_scale_offset(r_, g_)] == 127).all()
+            assert (P[1, :, [o.chunk_data_offset(r_, g_, t, b) for t in range(4) for b in range(4)]] == 0).all()
+    for r_ in range(128):
+        assert (P[:, 2, o.chunk_scale_offset(r_, 1)] == 127).all()  # k group 5 (k >= 160) of chunk kb=2
