@@ -116,26 +116,31 @@ int launch_tc(const void* A, const uint8_t* wpack, void* C, int M, int N, int K,
 
 // ------------------------------------------------------------------ small-M launch
 struct GvPlan {
-  int nt, ks, kbps, smem;
+  int nt, ks, kbps, stages, smem;
 };
 
+int env_knob(const char* name) {
+  const char* e = std::getenv(name);
+  return e ? std::atoi(e) : 0;
+}
+
+// Decode plan: the K-split (cluster size) and ring depth.  Enough CTAs to fill every SM
+// twice and each CTA's K range at most 2048 (32 chunks) so the staged activations stay
+// small.  Two ring stages (35 KB): measured on B200, more resident CTAs (more compute warps
+// per SM) beat a deeper ring at every decode shape.
 GvPlan plan_gemv(int M, int N, int K, int sm_count) {
   GvPlan p;
   p.nt = M <= 8 ? 1 : 2;
   const int nb = n_blocks_of(N), kb = k_blocks_of(K);
-  const int x_per_kb = 2 * (8 * p.nt) * 64;
-  const int fixed = p.nt == 1 ? GvCfg<1>::kOffX : GvCfg<2>::kOffX;
   p.ks = 1;
-  // K-split across the cluster until there are ~3 CTAs per SM and each CTA's K range is at
-  // most 2048 (32 chunks), so the staged activations stay small and 2-3 CTAs fit on an SM
-  while (p.ks < 8 && (nb * p.ks < 3 * sm_count || ceil_div(kb, p.ks) > 32)) p.ks *= 2;
-  static const int ks_override = [] {
-    const char* e = std::getenv("MXFP4_GEMV_KS");  // tuning knob: force the K-split (1, 2, 4, 8)
-    return e ? std::atoi(e) : 0;
-  }();
-  if (ks_override == 1 || ks_override == 2 || ks_override == 4 || ks_override == 8) p.ks = ks_override;
+  while (p.ks < 8 && (nb * p.ks < 2 * sm_count || ceil_div(kb, p.ks) > 32)) p.ks *= 2;
+  p.stages = 2;
+  // tuning knobs (sweeps only): force the K-split (1, 2, 4, 8) or the ring depth (2..8)
+  static const int ks_knob = env_knob("MXFP4_GEMV_KS"), st_knob = env_knob("MXFP4_GEMV_STAGES");
+  if (ks_knob == 1 || ks_knob == 2 || ks_knob == 4 || ks_knob == 8) p.ks = ks_knob;
+  if (st_knob >= 2 && st_knob <= kGvMaxStages) p.stages = st_knob;
   p.kbps = ceil_div(kb, p.ks);
-  p.smem = fixed + p.kbps * x_per_kb;
+  p.smem = p.nt == 1 ? GvCfg<1>::smem_bytes(p.stages, p.kbps, M) : GvCfg<2>::smem_bytes(p.stages, p.kbps, M);
   return p;
 }
 
@@ -162,7 +167,7 @@ int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, in
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, OutT>, static_cast<const __nv_bfloat16*>(A), M, K,
-                                     wpack, k_blocks_of(K), p.kbps, static_cast<OutT*>(C), N);
+                                     wpack, k_blocks_of(K), p.kbps, p.stages, static_cast<OutT*>(C), N);
   return ret(e);
 }
 
