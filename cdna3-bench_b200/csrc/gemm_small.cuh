@@ -27,7 +27,7 @@
 namespace mxb {
 
 #ifndef MXFP4_GV_MINB
-#define MXFP4_GV_MINB 1
+#define MXFP4_GV_MINB 4
 #endif
 #ifndef MXFP4_GV_MMA_VOLATILE
 #define MXFP4_GV_MMA_VOLATILE 0
@@ -45,10 +45,10 @@ template <int NT>
 struct GvCfg {
   static constexpr int kMP = 8 * NT;  // padded activation rows
   // [ring: stages x kGvStageBytes; reused for the partial sums once drained][full/empty
-  // barriers][xshift, abort][staged x: two 32-groups x M rows x 16 f16 pairs per chunk]
+  // barriers][xshift, abort, xmax][staged x: two 32-groups x M rows x 16 f16 pairs per chunk]
   __host__ __device__ static int off_bar(int stages) { return stages * kGvStageBytes; }
   __host__ __device__ static int off_shift(int stages) { return off_bar(stages) + 2 * kGvMaxStages * 8; }
-  __host__ __device__ static int off_x(int stages) { return (off_shift(stages) + 4 * kMP + 16 + 127) & ~127; }
+  __host__ __device__ static int off_x(int stages) { return (off_shift(stages) + 8 * kMP + 16 + 127) & ~127; }
   __host__ __device__ static int smem_bytes(int stages, int kb_per_split, int M) {
     return off_x(stages) + kb_per_split * 2 * M * 64;
   }
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
   uint64_t* empty = full + kGvMaxStages;
   int* xshift = reinterpret_cast<int*>(smem + Cfg::off_shift(stages));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(xshift + MP);
+  unsigned* xmax = reinterpret_cast<unsigned*>(xshift + MP + 4);  // per-row max |x| (float bits)
   float* red = reinterpret_cast<float*>(smem);  // aliases the drained ring
   uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Cfg::off_x(stages));
 
@@ -124,6 +125,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (threadIdx.x < MP) xmax[threadIdx.x] = 0u;
   __syncthreads();
 
   if (warp == 8) {
@@ -153,59 +155,79 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
   } else {
     const int g = lane >> 2, t = lane & 3;
     // ------------------------------------------------------------ stage activations (f16)
-    // Warp w stages rows w, w+8, ... of this CTA's K range.  Pass 1: the row's max |x|.
-    // Pass 2: re-read (L1 hits), scale by 2**shift (two exact power-of-two products, so any
-    // shift in range is exact) and convert to f16 pairs.  Layout: block (grp, m, t) of 16 bytes
-    // holds pairs t, t+4, t+8, t+12 of group grp for row m, stored at block position
-    // (grp*M + m)*4 + (t ^ (grp & 3)) so that the word stores spread over the banks.  Only
-    // the M real rows are staged; the MMA lanes of padding rows use zero registers.
+    // The 256 compute threads split this CTA's K range; each handles all M rows of its
+    // columns.  Pass 1: per-row max |x| (warp reduction, then one shared atomicMax on the
+    // float bits, which orders like the values for non-negative floats).  Pass 2: re-read
+    // (L1 hits), scale by 2**shift (two exact power-of-two products, so every shift in range
+    // is exact) and convert to f16 pairs.  Layout: block (grp, m, t) of 16 bytes holds pairs
+    // t, t+4, t+8, t+12 of group grp for row m, stored at block position
+    // (grp*M + m)*4 + (t ^ (grp & 3)) so that the word stores spread over the banks.  Only the
+    // M real rows are staged; the MMA lanes of padding rows use zero registers.
     if (!(MXFP4_GV_DIAG & 8)) {
       const int k_lo = kb0 * 64;
       const int nvec = nkb * 8;  // 16-byte vectors (8 bf16) per row in the staged range
-      for (int m = warp; m < MP; m += 8) {
-        const __nv_bfloat16* arow = A + static_cast<size_t>(m) * K;
-        int shift = 0;
-        if (m < M) {
-          float amax = 0.0f;
-#pragma unroll 8
-          for (int v = lane; v < nvec; v += 32) {
-            const int k = k_lo + v * 8;
-            if (k < K) {
-              const uint4 raw = *reinterpret_cast<const uint4*>(arow + k);
-              const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      const __nv_bfloat16* a_lo = A + k_lo;
+      float am[MP];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                amax = fmaxf(amax, fabsf(__uint_as_float(w[i] << 16)));
-                amax = fmaxf(amax, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
-              }
+      for (int m = 0; m < MP; ++m) am[m] = 0.0f;
+      for (int v = threadIdx.x; v < nvec; v += 256) {
+        const bool kin = k_lo + v * 8 < K;
+#pragma unroll
+        for (int m = 0; m < MP; ++m)
+          if (m < M && kin) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(a_lo + static_cast<size_t>(m) * K + v * 8);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              am[m] = fmaxf(am[m], fabsf(__uint_as_float(w[i] << 16)));
+              am[m] = fmaxf(am[m], fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
             }
           }
+      }
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-          if (amax > 0.0f && amax <= 3.0e38f) {
-            int E;
-            frexpf(amax, &E);
-            shift = 15 - E;  // the row max lands in [2^14, 2^15)
-          }
-        }
-        if (lane == 0) xshift[m] = shift;
-        if (m >= M) continue;
-        const float f1 = exp2i(shift / 2), f2 = exp2i(shift - shift / 2);
-#pragma unroll 4
-        for (int v = lane; v < nvec; v += 32) {
-          const int k = k_lo + v * 8;
-          uint4 raw = make_uint4(0, 0, 0, 0);
-          if (k < K) raw = *reinterpret_cast<const uint4*>(arow + k);
-          const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-          const int grp = v >> 2, slot = v & 3;  // vector v = pairs 4*slot .. 4*slot+3 of group grp
-          const uint32_t blk = smem_u32(xs + (grp * M + m) * 16 + slot);
+      for (int m = 0; m < MP; ++m)
+        if (m < M) {
+          float a = am[m];
 #pragma unroll
-          for (int tt = 0; tt < 4; ++tt) {
-            const float lo = __uint_as_float(w[tt] << 16) * f1 * f2;
-            const float hi = __uint_as_float(w[tt] & 0xFFFF0000u) * f1 * f2;
-            sts32(blk + (tt ^ (grp & 3)) * 16, f16x2_from(lo, hi));
-          }
+          for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+          if (lane == 0 && a > 0.0f) atomicMax(xmax + m, __float_as_uint(a));
         }
+      named_bar_sync(1, 256);
+      if (threadIdx.x < MP) {
+        const float amax = __uint_as_float(xmax[threadIdx.x]);
+        int shift = 0;
+        if (threadIdx.x < M && amax > 0.0f && amax <= 3.0e38f) {
+          int E;
+          frexpf(amax, &E);
+          shift = 15 - E;  // the row max lands in [2^14, 2^15)
+        }
+        xshift[threadIdx.x] = shift;
+      }
+      named_bar_sync(1, 256);
+      float f1[MP], f2[MP];
+#pragma unroll
+      for (int m = 0; m < MP; ++m) {
+        const int sh = xshift[m];
+        f1[m] = exp2i(sh / 2);
+        f2[m] = exp2i(sh - sh / 2);
+      }
+      for (int v = threadIdx.x; v < nvec; v += 256) {
+        const bool kin = k_lo + v * 8 < K;
+        const int grp = v >> 2, slot = v & 3;  // vector v = pairs 4*slot .. 4*slot+3 of group grp
+#pragma unroll
+        for (int m = 0; m < MP; ++m)
+          if (m < M) {
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (kin) raw = *reinterpret_cast<const uint4*>(a_lo + static_cast<size_t>(m) * K + v * 8);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+            const uint32_t blk = smem_u32(xs + (grp * M + m) * 16 + slot);
+#pragma unroll
+            for (int tt = 0; tt < 4; ++tt) {
+              const float lo = __uint_as_float(w[tt] << 16) * f1[m] * f2[m];
+              const float hi = __uint_as_float(w[tt] & 0xFFFF0000u) * f1[m] * f2[m];
+              sts32(blk + (tt ^ (grp & 3)) * 16, f16x2_from(lo, hi));
+            }
+          }
       }
     }
     named_bar_sync(1, 256);
@@ -219,10 +241,19 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     const uint32_t xs_a = smem_u32(xs);
     const uint32_t lane_d = (32 * warp + lane) * 16;
     const uint32_t lane_s = kChunkData + (8 * warp + g) * 4;
+    // activation block of (group xg, row 8*jt + g) for this lane: lane_x[xg & 3] + xg*M*64 + jt*512
+    uint32_t lane_x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) lane_x[j] = xs_a + g * 64 + (t ^ j) * 16;
+    const uint32_t m64 = static_cast<uint32_t>(M) * 64;
+    bool row_live[NT];
+#pragma unroll
+    for (int jt = 0; jt < NT; ++jt) row_live[jt] = 8 * jt + g < M;
     for (int i = 0; i < nst; ++i) {
       const int s = i % stages;
       if (!warp_wait(&full[s], (i / stages) & 1, kErrWaitFull, abort_flag)) break;
       const uint32_t st = ring_a + s * kGvStageBytes;
+      const uint32_t xstage = static_cast<uint32_t>(i) * (2 * kGvStageChunks) * m64;
 #pragma unroll
       for (int c = 0; c < kGvStageChunks; ++c) {
         const int ci = i * kGvStageChunks + c;
@@ -230,13 +261,16 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
           const uint4 d = lds128(st + c * kChunkBytes + lane_d);
           const uint32_t sw = lds32(st + c * kChunkBytes + lane_s);
           const uint32_t wv[4] = {d.x, d.y, d.z, d.w};  // (g,G0) (g+8,G0) (g,G1) (g+8,G1)
+          // scale bytes (g,G0) (g+8,G0) (g,G1) (g+8,G1) -> 2**(s-127) as f32 bits (s << 23);
+          // a zero byte (2**-127) decodes to 0, a difference far below the error bound.
+          const float sc[4] = {__uint_as_float((sw << 23) & 0x7F800000u), __uint_as_float((sw << 15) & 0x7F800000u),
+                               __uint_as_float((sw << 7) & 0x7F800000u), __uint_as_float((sw >> 1) & 0x7F800000u)};
 #pragma unroll
           for (int G = 0; G < 2; ++G) {
 #if MXFP4_GV_DIAG & 2
             const float sl = 1.0f, sh = __uint_as_float(sw);
 #else
-            const float sl = e8m0_to_f32((sw >> (16 * G)) & 0xFF);
-            const float sh = e8m0_to_f32((sw >> (16 * G + 8)) & 0xFF);
+            const float sl = sc[2 * G], sh = sc[2 * G + 1];
 #endif
             uint32_t fl[4], fh[4];
 #if MXFP4_GV_DIAG & 1
@@ -246,11 +280,11 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
             e2m1x8_to_f16x2(wv[2 * G], fl);
             e2m1x8_to_f16x2(wv[2 * G + 1], fh);
 #endif
-            const int xg = 2 * ci + G;
+            const int xl = 2 * c + G;  // group index within the stage; (2*ci + G) & 3 == xl & 3
 #pragma unroll
             for (int jt = 0; jt < NT; ++jt) {
               uint4 xb = make_uint4(0, 0, 0, 0);
-              if (8 * jt + g < M) xb = lds128(xs_a + (((xg * M + 8 * jt + g) * 4 + (t ^ (xg & 3))) * 4) * 4);
+              if (row_live[jt]) xb = lds128(lane_x[xl & 3] + xstage + xl * m64 + jt * 512);
               float dd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #if MXFP4_GV_DIAG & 4
               dd[0] = __uint_as_float((fl[0] ^ fh[1] ^ fl[2] ^ fh[3] ^ xb.x ^ xb.w) & 0x3fffffff);
