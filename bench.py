@@ -76,7 +76,14 @@ def parse():
 def shapes_for(workload: str, world: int):
     M, gemms = WORKLOADS[workload]
     if workload == "tp_sweep":  # strong scaling: the fixed layer is split column-wise
-        return M, [(n, N // world, K) for n, N, K in gemms]
+        from mxfp4_b200.sharding import column_slice
+
+        rank = int(os.environ.get("RANK", "0"))
+        out = []
+        for n, N, K in gemms:
+            n0, n1 = column_slice(N, world, rank)
+            out.append((n, n1 - n0, K))
+        return M, out
     return M, gemms
 
 
@@ -281,7 +288,11 @@ def main():
 
     gather = None
     if world > 1 and (args.allgather or args.workload == "tp_sweep"):
-        gather = [torch.empty((world, M, it["N"]), dtype=torch.bfloat16, device=dev) for it in items]
+        from mxfp4_b200.sharding import all_gather_columns
+
+        full_n = [N for _, N, _ in WORKLOADS[args.workload][1]] if args.workload == "tp_sweep" \
+            else [world * it["N"] for it in items]
+        gather = lambda j, Y: all_gather_columns(Y, full_n[j])  # noqa: E731
 
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
           for _ in range(args.steps)]
@@ -295,7 +306,7 @@ def main():
             if record:
                 ev[i_step][j][1].record()
             if gather is not None:
-                dist.all_gather_into_tensor(gather[j], it["C"])
+                gather(j, it["C"])
 
     for i in range(args.warmup):
         step(i, False)
