@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="all-gather outputs (column-parallel)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="decode workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
     return ap.parse_args()
 
 
@@ -311,6 +313,31 @@ def main():
     for i in range(args.warmup):
         step(i, False)
     barrier()
+
+    # Decode GEMMs last ~10-60 us, about the host cost of a Python launch: a serving loop
+    # replays them from a CUDA graph, and so does the bench (one graph per weight rotation,
+    # with timing events recorded as graph nodes around every GEMM).
+    graphs = None
+    if decode and not args.no_graph and gather is None:
+        graphs, gev = [], []
+        for r in range(rot):
+            evs = [(torch.cuda.Event(enable_timing=True, external=True),
+                    torch.cuda.Event(enable_timing=True, external=True)) for _ in items]
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for j, it in enumerate(items):
+                    evs[j][0].record()
+                    mx.gemm(it["A"], it["w_rot"][r], C=it["C"])
+                    evs[j][1].record()
+            graphs.append(g)
+            gev.append(evs)
+        for r in range(rot):
+            graphs[r].replay()
+        barrier()
+
+        def step(i_step: int, record: bool):  # noqa: F811
+            graphs[i_step % rot].replay()
+
     sampler = ClockSampler(local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
@@ -322,8 +349,12 @@ def main():
         barrier()
     total_ms = t0.elapsed_time(t1)
     assert mx.device_error() == 0, "a kernel recorded a device error"
-    launch_ms = [statistics.mean(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(args.steps))
-                 for j in range(len(items))]
+    if graphs is None:
+        launch_ms = [statistics.mean(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(args.steps))
+                     for j in range(len(items))]
+    else:  # each graph's events hold its last replay inside the timed region
+        launch_ms = [statistics.mean(gev[r][j][0].elapsed_time(gev[r][j][1]) for r in range(min(rot, args.steps)))
+                     for j in range(len(items))]
     ms_step = max_over_ranks(total_ms / args.steps)
     value = world * units_step / (ms_step * 1e-3) / scale
 
@@ -378,6 +409,7 @@ def main():
                 "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if decode
                        else "inputs larger than L2: one step touches "
                             f"{(bytes_step + sum(M * it['N'] * 2 for it in items)) / 1e6:.0f} MB"),
+                "launch": "one CUDA graph per step" if graphs is not None else "eager, one launch per GEMM",
                 "parallelism": (f"tp{world} column-parallel + NCCL all-gather" if gather is not None
                                 else f"weak x{world}, per-rank N-slice, no collective"),
             },
