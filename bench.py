@@ -414,7 +414,8 @@ def main():
                                 else f"weak x{world}, per-rank N-slice, no collective"),
             },
             "roofline": roof, "per_gemm": per_gemm, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": len(items) * args.steps, "clocks": sampler.summary(),
+            "gpu_launches": args.steps * sum(1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
+                                             for it in items), "clocks": sampler.summary(),
         }), flush=True)
     if world > 1:
         dist.destroy_process_group()

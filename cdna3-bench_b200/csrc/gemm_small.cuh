@@ -47,7 +47,7 @@ struct GvCfg {
   // [ring: stages x kGvStageBytes; reused for the partial sums once drained][full/empty
   // barriers][xshift, abort, xmax][staged x: two 32-groups x M rows x 16 f16 pairs per chunk]
   __host__ __device__ static int off_bar(int stages) { return stages * kGvStageBytes; }
-  __host__ __device__ static int off_shift(int stages) { return off_bar(stages) + 2 * kGvMaxStages * 8; }
+  __host__ __device__ static int off_shift(int stages) { return off_bar(stages) + (2 * kGvMaxStages + 2) * 8; }
   __host__ __device__ static int off_x(int stages) { return (off_shift(stages) + 8 * kMP + 16 + 127) & ~127; }
   __host__ __device__ static int smem_bytes(int stages, int kb_per_split, int M) {
     return off_x(stages) + kb_per_split * 2 * M * 64;
@@ -96,13 +96,15 @@ __device__ __forceinline__ __nv_bfloat16 gv_out<__nv_bfloat16>(float v) { return
 template <int NT, typename OutT>
 __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     gemv_kernel(const __nv_bfloat16* __restrict__ A, int M, int K, const uint8_t* __restrict__ wpack,
-                int k_blocks, int kb_per_split, int stages, OutT* __restrict__ C, int N) {
+                int k_blocks, int kb_per_split, int stages, OutT* __restrict__ C, int N,
+                const uint8_t* __restrict__ xpre, const int* __restrict__ xpre_shift) {
   using Cfg = GvCfg<NT>;
   constexpr int MP = Cfg::kMP;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::off_bar(stages));
   uint64_t* empty = full + kGvMaxStages;
+  uint64_t* xbar = empty + kGvMaxStages;  // prestaged activations landed
   int* xshift = reinterpret_cast<int*>(smem + Cfg::off_shift(stages));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(xshift + MP);
   unsigned* xmax = reinterpret_cast<unsigned*>(xshift + MP + 4);  // per-row max |x| (float bits)
@@ -122,6 +124,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 8);
     }
+    mbar_init(xbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -134,7 +137,20 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
       const uint8_t* src = wpack + (static_cast<size_t>(nb) * k_blocks + kb0) * kChunkBytes;
       uint32_t pend = 0, pend_ph = 0;
       bool aborted = false;
+      // Prestaged activations (written by the launch just before this one): the weight
+      // stages that need no free slot go out first, then -- once that launch has finished --
+      // one bulk copy of this CTA's slice of the staged activations.
+      const uint32_t xbytes = static_cast<uint32_t>(nkb) * 2 * M * 64;
+      const int x_at = min(stages, nst);
+      bool x_pending = xpre != nullptr && xbytes > 0;
+      auto issue_x = [&]() {
+        griddep_wait();
+        mbar_arrive_expect_tx(xbar, xbytes);
+        bulk_load(xs, xpre + static_cast<size_t>(kb0) * 2 * M * 64, xbytes, xbar);
+        x_pending = false;
+      };
       for (int i = 0; i < nst; ++i) {
+        if (x_pending && i == x_at) issue_x();
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
@@ -147,6 +163,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
         pend |= 1u << s;
         pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
       }
+      if (x_pending) issue_x();  // also when aborted: the consumers may be waiting on it
       if (aborted)
         for (int i = 0; i < stages; ++i)
           if ((pend >> i) & 1) mbar_wait_drain(&full[i], (pend_ph >> i) & 1);
@@ -161,9 +178,15 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     // (L1 hits), scale by 2**shift (two exact power-of-two products, so every shift in range
     // is exact) and convert to f16 pairs.  Layout: block (grp, m, t) of 16 bytes holds pairs
     // t, t+4, t+8, t+12 of group grp for row m, stored at block position
-    // (grp*M + m)*4 + (t ^ (grp & 3)) so that the word stores spread over the banks.  Only the
-    // M real rows are staged; the MMA lanes of padding rows use zero registers.
-    if (!(MXFP4_GV_DIAG & 8)) {
+    // (grp*M + m)*4 + (t ^ (kg & 3)), kg = 2*kb0 + grp the group's index along all of K, so that
+    // the word stores spread over the banks (the prestaged layout of gemv_prestage_kernel is the
+    // same with kg in place of grp).  Only the M real rows are staged; the MMA lanes of padding
+    // rows use zero registers.
+    if (xpre != nullptr) {
+      griddep_wait();
+      if (threadIdx.x < MP) xshift[threadIdx.x] = threadIdx.x < M ? xpre_shift[threadIdx.x] : 0;
+      if (nkb > 0) warp_wait(xbar, 0, kErrWaitFull, abort_flag);
+    } else if (!(MXFP4_GV_DIAG & 8)) {
       const int k_lo = kb0 * 64;
       const int nvec = nkb * 8;  // 16-byte vectors (8 bf16) per row in the staged range
       const __nv_bfloat16* a_lo = A + k_lo;
@@ -225,7 +248,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
             for (int tt = 0; tt < 4; ++tt) {
               const float lo = __uint_as_float(w[tt] << 16) * f1[m] * f2[m];
               const float hi = __uint_as_float(w[tt] & 0xFFFF0000u) * f1[m] * f2[m];
-              sts32(blk + (tt ^ (grp & 3)) * 16, f16x2_from(lo, hi));
+              sts32(blk + (tt ^ ((grp + 2 * kb0) & 3)) * 16, f16x2_from(lo, hi));
             }
           }
       }
@@ -241,10 +264,10 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     const uint32_t xs_a = smem_u32(xs);
     const uint32_t lane_d = (32 * warp + lane) * 16;
     const uint32_t lane_s = kChunkData + (8 * warp + g) * 4;
-    // activation block of (group xg, row 8*jt + g) for this lane: lane_x[xg & 3] + xg*M*64 + jt*512
+    // activation block of (local group xg, row 8*jt + g) for this lane: lane_x[xg & 3] + xg*M*64 + jt*512
     uint32_t lane_x[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) lane_x[j] = xs_a + g * 64 + (t ^ j) * 16;
+    for (int j = 0; j < 4; ++j) lane_x[j] = xs_a + g * 64 + (t ^ ((j + 2 * kb0) & 3)) * 16;
     const uint32_t m64 = static_cast<uint32_t>(M) * 64;
     bool row_live[NT];
 #pragma unroll
@@ -327,6 +350,63 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     if (n < N) C[static_cast<size_t>(m) * N + n] = gv_out<OutT>(sum);
   }
   cluster_sync_all();
+}
+
+// Activation staging done once per GEMM for the decode kernel (used when the caller gives
+// workspace for it): one CTA per activation row computes the row's max |x| over all of K, a
+// power-of-two shift that puts it in [2^14, 2^15), and writes the row as f16 pairs in the
+// layout gemv_kernel stages into shared memory, over all k_blocks*64 columns (zeros past K):
+// 16-byte block (kg, m, t), kg the 32-group index along K, at block position
+// (kg*M + m)*4 + (t ^ (kg & 3)), holding pairs t, t+4, t+8, t+12 of the group.  Each decode
+// CTA then fetches its K range with one bulk copy instead of converting it again.  The
+// dependent decode launch may start as soon as every CTA here has begun.
+__global__ void __launch_bounds__(256) gemv_prestage_kernel(const __nv_bfloat16* __restrict__ A, int M, int K,
+                                                            int k_blocks, uint8_t* __restrict__ xpre,
+                                                            int* __restrict__ xpre_shift) {
+  griddep_launch_dependents();
+  __shared__ float wmax[8];
+  const int m = blockIdx.x;
+  const int nvec = k_blocks * 8;
+  const __nv_bfloat16* arow = A + static_cast<size_t>(m) * K;
+  float amax = 0.0f;
+  for (int v = threadIdx.x; v < nvec; v += 256)
+    if (v * 8 < K) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(arow + v * 8);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[i] << 16)));
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
+      }
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, wmax[i]);
+  int shift = 0;
+  if (amax > 0.0f && amax <= 3.0e38f) {
+    int E;
+    frexpf(amax, &E);
+    shift = 15 - E;
+  }
+  if (threadIdx.x == 0) xpre_shift[m] = shift;
+  const float f1 = exp2i(shift / 2), f2 = exp2i(shift - shift / 2);
+  for (int v = threadIdx.x; v < nvec; v += 256) {
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (v * 8 < K) raw = *reinterpret_cast<const uint4*>(arow + v * 8);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const int kg = v >> 2, slot = v & 3;
+    uint32_t* blk = reinterpret_cast<uint32_t*>(xpre) + (static_cast<size_t>(kg) * M + m) * 16 + slot;
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+      const float lo = __uint_as_float(w[tt] << 16) * f1 * f2;
+      const float hi = __uint_as_float(w[tt] & 0xFFFF0000u) * f1 * f2;
+      blk[(tt ^ (kg & 3)) * 4] = f16x2_from(lo, hi);
+    }
+  }
 }
 
 }  // namespace mxb

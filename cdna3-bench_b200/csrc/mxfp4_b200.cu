@@ -146,7 +146,7 @@ GvPlan plan_gemv(int M, int N, int K, int sm_count) {
 
 template <int NT, typename OutT>
 int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, int K, const GvPlan& p,
-                  cudaStream_t stream, DeviceState* d) {
+                  cudaStream_t stream, DeviceState* d, const uint8_t* xpre, const int* xpre_shift) {
   const int slot = (NT == 1 ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
   if (!d->gv_attr[slot]) {
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -159,27 +159,53 @@ int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, in
   cfg.blockDim = dim3(kGvThreads, 1, 1);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = p.ks;
   attr[0].val.clusterDim.z = 1;
+  // With prestaged activations the launch before this one is our own prestage kernel, which
+  // writes nothing this kernel reads before griddep_wait(): let it start early.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = xpre ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, OutT>, static_cast<const __nv_bfloat16*>(A), M, K,
-                                     wpack, k_blocks_of(K), p.kbps, p.stages, static_cast<OutT*>(C), N);
+                                     wpack, k_blocks_of(K), p.kbps, p.stages, static_cast<OutT*>(C), N,
+                                     xpre, xpre_shift);
   return ret(e);
 }
 
+// Bytes of decode-kernel workspace for activations staged once per GEMM (0 when the decode
+// kernel stages them itself): f16 [k_blocks*64] x M plus M row shifts.
+size_t gemv_prestage_bytes(int M, int N, int K) {
+  (void)N;
+  static const int knob = env_knob("MXFP4_GEMV_PRESTAGE");  // sweeps: -1 never, 1 always
+  const int min_m = knob < 0 ? 1 << 30 : (knob > 0 ? 1 : 4);
+  if (M < min_m || M > 16) return 0;
+  return static_cast<size_t>(k_blocks_of(K)) * 128 * M + 256;
+}
+
 int launch_gemv(const void* A, const uint8_t* wpack, void* C, int c_dtype, int M, int N, int K,
-                cudaStream_t stream, DeviceState* d) {
+                cudaStream_t stream, DeviceState* d, uint8_t* xws, size_t xws_bytes) {
   const GvPlan p = plan_gemv(M, N, K, d->sm_count);
   if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  const size_t need = gemv_prestage_bytes(M, N, K);
+  uint8_t* xpre = nullptr;
+  int* xshift = nullptr;
+  if (need && xws && xws_bytes >= need && aligned16(xws)) {
+    xpre = xws;
+    xshift = reinterpret_cast<int*>(xws + need - 256);
+    gemv_prestage_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, k_blocks_of(K), xpre,
+                                                xshift);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ret(e);
+  }
   if (p.nt == 1)
-    return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<1, float>(A, wpack, C, M, N, K, p, stream, d)
-                                      : launch_gemv_t<1, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d);
-  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<2, float>(A, wpack, C, M, N, K, p, stream, d)
-                                    : launch_gemv_t<2, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d);
+    return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<1, float>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift)
+                                      : launch_gemv_t<1, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift);
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<2, float>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift)
+                                    : launch_gemv_t<2, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift);
 }
 
 size_t prepacked_bytes(int N, int K) {
@@ -351,9 +377,10 @@ int mxfp4_shape_supported(int path, int M, int N, int K) {
 }
 
 size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
-  (void)M;
-  if (N <= 0 || K <= 0) return 0;
-  return layout == MXFP4_LAYOUT_PREPACKED ? 0 : prepacked_bytes(N, K);
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const size_t pre = layout == MXFP4_LAYOUT_PREPACKED ? 0 : (prepacked_bytes(N, K) + 255) / 256 * 256;
+  const size_t x = gemv_prestage_bytes(M, N, K);  // M <= 16: the decode path may serve the call
+  return pre + x;
 }
 
 int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype, int M, int N,
@@ -371,6 +398,8 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
   if (rc) return rc;
   auto s = static_cast<cudaStream_t>(stream);
   const uint8_t* wpack = B;
+  uint8_t* rest = static_cast<uint8_t*>(workspace);  // workspace left after the re-laid weights
+  size_t rest_bytes = workspace ? workspace_bytes : 0;
   if (layout != MXFP4_LAYOUT_PREPACKED) {
     const size_t need = prepacked_bytes(N, K);
     if (!workspace || workspace_bytes < need) return MXFP4_ERR_WORKSPACE;
@@ -379,6 +408,9 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
     rc = do_prepack(B, B_scales, N, K, layout, static_cast<uint8_t*>(workspace), s);
     if (rc) return rc;
     wpack = static_cast<const uint8_t*>(workspace);
+    const size_t used = (need + 255) / 256 * 256;
+    rest = workspace_bytes > used ? static_cast<uint8_t*>(workspace) + used : nullptr;
+    rest_bytes = workspace_bytes > used ? workspace_bytes - used : 0;
   }
   switch (path) {
     case MXFP4_PATH_TC:
@@ -387,7 +419,7 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
     case MXFP4_PATH_TC_SMEM:
       return c_dtype == MXFP4_DTYPE_F32 ? launch_tc<false, float>(A, wpack, C, M, N, K, s, d)
                                         : launch_tc<false, __nv_bfloat16>(A, wpack, C, M, N, K, s, d);
-    case MXFP4_PATH_GEMV: return launch_gemv(A, wpack, C, c_dtype, M, N, K, s, d);
+    case MXFP4_PATH_GEMV: return launch_gemv(A, wpack, C, c_dtype, M, N, K, s, d, rest, rest_bytes);
     default: return MXFP4_ERR_INVALID_ARGUMENT;
   }
 }

@@ -163,7 +163,7 @@ class MXFP4Weight:
         return self.N * self.K // 2 + self.N * self.K // _GROUP
 
 
-_LAYOUTS = {"ref": _lib.LAYOUT_REF, "nk": _lib.LAYOUT_NK, "g": _lib.LAYOUT_G}
+_LAYOUTS = {"ref": _lib.LAYOUT_REF, "nk": _lib.LAYOUT_NK, "g": _lib.LAYOUT_G, "prepacked": _lib.LAYOUT_PREPACKED}
 
 
 def prepack_b200(B_packed, B_scales, layout: str = "ref", N: int | None = None, K: int | None = None):
@@ -216,10 +216,14 @@ def gemm(A: torch.Tensor, w: MXFP4Weight, out_dtype=torch.bfloat16, path: str = 
     if C is None:
         C = torch.empty((M, w.N), dtype=out_dtype, device=A.device)
     _check(C.is_cuda and C.dtype in _ODT and tuple(C.shape) == (M, w.N) and C.is_contiguous(), "C shape/contig")
+    L = _lib.lib()
+    # decode shapes: room for the activations converted once per call (torch's caching allocator)
+    nws = L.mxfp4_gemm_workspace_bytes(M, w.N, w.K, _lib.LAYOUT_PREPACKED)
+    ws = torch.empty(nws, dtype=torch.uint8, device=A.device) if nws else None
     _lib.check(
-        _lib.lib().mxfp4_gemm(
+        L.mxfp4_gemm(
             _ptr(A), _ptr(w.data), None, _ptr(C), _ODT[C.dtype], M, w.N, w.K,
-            _lib.LAYOUT_PREPACKED, _lib.PATH_NAMES[path], None, 0, _stream(),
+            _lib.LAYOUT_PREPACKED, _lib.PATH_NAMES[path], _ptr(ws) if ws is not None else None, nws, _stream(),
         ),
         "mxfp4_gemm",
     )

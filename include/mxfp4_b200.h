@@ -119,14 +119,18 @@ int mxfp4_select_path(int M, int N, int K);
  * (csrc/common.h:80-99): every path here needs K % 32 == 0 and N % 8 == 0. */
 int mxfp4_shape_supported(int path, int M, int N, int K);
 
-/* Workspace bytes mxfp4_gemm needs for a weight layout (0 for MXFP4_LAYOUT_PREPACKED; the
- * prepacked copy of B for the other layouts). */
+/* Workspace bytes mxfp4_gemm uses for a weight layout: the prepacked copy of B for layouts
+ * other than PREPACKED (required), plus, for M <= 16 (shapes the decode path may serve), room for the
+ * activations converted once per call (optional: with less workspace every decode CTA converts
+ * its own slice, which is slower for M >= 4). */
 size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout);
 
 /* C[M,N] = A[M,K] (bf16) * dequant(B)[K,N], fp32 accumulation, C in c_dtype.
  * Replaces the launcher ABI launch_strategy_{a..m} (csrc/common.h:43-78) and the dispatch
  * in csrc/mxfp4_ext.cpp:36-48; the reference always writes fp32 C, this adds bf16.
- * For layouts other than PREPACKED the weights are first re-laid into `workspace`. */
+ * For layouts other than PREPACKED the weights are first re-laid into `workspace`; any room
+ * left after them (see mxfp4_gemm_workspace_bytes) serves the decode path's staged activations.
+ * Calls sharing one workspace must not overlap on the GPU. */
 int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
                int M, int N, int K, int layout, int path, void* workspace, size_t workspace_bytes,
                void* stream);

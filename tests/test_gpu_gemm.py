@@ -135,3 +135,33 @@ def test_decode_full_size_against_library_gemm(mx):
     ref = A.float() @ mx.dequantize_mxfp4(Bp, Bs, axis=0)
     C = mx.gemm(A, w, path="gemv").float()
     assert ((C - ref).abs().max() / ref.abs().max()).item() <= TOL
+
+
+@pytest.mark.parametrize("M", [4, 16])
+def test_gemv_without_workspace_stages_in_kernel(mx, M):
+    """Through the C ABI with no workspace the decode kernel converts the activations itself
+    (the path a caller without spare device memory gets); same result bound."""
+    import ctypes
+
+    from mxfp4_b200 import _lib
+
+    N, K = 640, 4096
+    A, Bp, Bs = make_case(M, N, K, seed=11 + M)
+    ref = o.ref_gemm(A, Bp, Bs)
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).to(torch.bfloat16).cuda()
+    outs = []
+    for ws_bytes in (0, int(mx.workspace_bytes(M, N, K, "prepacked"))):
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+        C = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        rc = _lib.lib().mxfp4_gemm(
+            ctypes.c_void_p(At.data_ptr()), ctypes.c_void_p(w.data.data_ptr()), None, ctypes.c_void_p(C.data_ptr()),
+            _lib.DTYPE_F32, M, N, K, _lib.LAYOUT_PREPACKED, _lib.PATH_GEMV,
+            ctypes.c_void_p(ws.data_ptr()) if ws_bytes else None, ws_bytes,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert mx.device_error() == 0
+        outs.append(C.cpu().numpy())
+        assert rel_err(outs[-1], ref) <= TOL
+    assert mx.workspace_bytes(M, N, K, "prepacked") > 0
