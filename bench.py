@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="all-gather outputs (column-parallel)")
+    ap.add_argument("--unfused", action="store_true",
+                    help="column-parallel: GEMM then a separate NCCL all-gather (default: all-gather fused "
+                         "into the GEMM epilogue, stores straight into every GPU's output over NVLink)")
     ap.add_argument("--no-graph", action="store_true",
                     help="decode workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
     return ap.parse_args()
@@ -239,6 +242,7 @@ def main():
     import torch.distributed as dist
 
     import mxfp4_b200 as mx
+    from mxfp4_b200 import kernels as kk
     from mxfp4_b200 import cost_model
 
     if not torch.cuda.is_available():
@@ -288,13 +292,20 @@ def main():
             it["w_rot"] = [it["w"]] + [mx.MXFP4Weight(it["w"].data.clone(), it["w"].N, it["w"].K)
                                        for _ in range(rot - 1)]
 
-    gather = None
+    gather = fused = None
     if world > 1 and (args.allgather or args.workload == "tp_sweep"):
         from mxfp4_b200.sharding import all_gather_columns
 
         full_n = [N for _, N, _ in WORKLOADS[args.workload][1]] if args.workload == "tp_sweep" \
             else [world * it["N"] for it in items]
         gather = lambda j, Y: all_gather_columns(Y, full_n[j])  # noqa: E731
+        fused = None
+        if not args.unfused:
+            from mxfp4_b200 import sharding
+
+            fused = [sharding.PeerOutput(M, full_n[j], torch.bfloat16) for j in range(len(items))]
+            offs = [sharding.column_slice(full_n[j], world, rank)[0] if args.workload == "tp_sweep"
+                    else rank * it["N"] for j, it in enumerate(items)]
 
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
           for _ in range(args.steps)]
@@ -304,10 +315,15 @@ def main():
             w = it["w_rot"][i_step % rot] if decode else it["w"]
             if record:
                 ev[i_step][j][0].record()
-            mx.gemm(it["A"], w, C=it["C"])
+            if fused is not None:
+                kk.gemm_allgather(it["A"], w, fused[j].ptrs, offs[j], fused[j].N)
+            else:
+                mx.gemm(it["A"], w, C=it["C"])
             if record:
                 ev[i_step][j][1].record()
-            if gather is not None:
+            if fused is not None:
+                fused[j].sync()
+            elif gather is not None:
                 gather(j, it["C"])
 
     for i in range(args.warmup):
@@ -410,7 +426,9 @@ def main():
                        else "inputs larger than L2: one step touches "
                             f"{(bytes_step + sum(M * it['N'] * 2 for it in items)) / 1e6:.0f} MB"),
                 "launch": "one CUDA graph per step" if graphs is not None else "eager, one launch per GEMM",
-                "parallelism": (f"tp{world} column-parallel + NCCL all-gather" if gather is not None
+                "parallelism": (f"tp{world} column-parallel, all-gather fused into the GEMM epilogue (NVLink "
+                                "stores into every GPU's output)" if fused is not None else
+                                f"tp{world} column-parallel + NCCL all-gather" if gather is not None
                                 else f"weak x{world}, per-rank N-slice, no collective"),
             },
             "roofline": roof, "per_gemm": per_gemm, "e2e": e2e, "cpu_baseline": cpu,

@@ -75,9 +75,19 @@ __device__ __forceinline__ void tc_tile_coords(int t, int m_blocks, int n_blocks
   nb = local / gm;
 }
 
+// Output destinations: the epilogue stores every output slab through each of these maps.  One
+// map is the plain GEMM; several give the all-gather form, where each map covers this GPU's
+// column slice of one GPU's full output buffer (its own, or a peer's over NVLink).
+constexpr int kMaxOutDst = 8;
+struct TcOut {
+  CUtensorMap map[kMaxOutDst];
+  int count;
+  int fence_sys;  // 1: make the stores visible system-wide before the kernel ends (peer buffers)
+};
+
 template <bool kTS, typename OutT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_out,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ TcOut out,
                    const uint8_t* __restrict__ wpack, int M, int k_blocks, int m_blocks, int n_blocks) {
   using Cfg = TcCfg<kTS, OutT>;
   constexpr int S = Cfg::kStages;
@@ -106,7 +116,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_act);
-    prefetch_tmap(&tm_out);
+    for (int d = 0; d < out.count; ++d) prefetch_tmap(&out.map[d]);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -242,7 +252,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tm_out, stage_ptr, n0, mc);
+              for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage_ptr, n0, mc);
               bulk_commit();
             }
           }
@@ -267,7 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&tm_out, stage_ptr, n0, mc);
+              for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage_ptr, n0, mc);
               bulk_commit();
             }
           }
@@ -275,7 +285,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       aph ^= 1;
     }
-    if (lane == 0) bulk_wait_all();
+    if (lane == 0) {
+      bulk_wait_all();
+      if (out.fence_sys) asm volatile("fence.acq_rel.sys;" ::: "memory");
+    }
   } else {
     // ------------------------------------------------------------ dequant
     const int q = warp & 3;

@@ -93,10 +93,18 @@ __device__ __forceinline__ float gv_out<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __nv_bfloat16 gv_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
+// Output destinations of the decode kernel: C[m, n] goes to p[d][m * ldc + n_off + n] for every
+// d < count (one destination for the plain GEMM; one per GPU for the all-gather form).
+template <typename OutT>
+struct GvOut {
+  OutT* p[8];
+  int count, ldc, n_off, fence_sys;
+};
+
 template <int NT, typename OutT>
 __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     gemv_kernel(const __nv_bfloat16* __restrict__ A, int M, int K, const uint8_t* __restrict__ wpack,
-                int k_blocks, int kb_per_split, int stages, OutT* __restrict__ C, int N,
+                int k_blocks, int kb_per_split, int stages, const GvOut<OutT> out, int N,
                 const uint8_t* __restrict__ xpre, const int* __restrict__ xpre_shift) {
   using Cfg = GvCfg<NT>;
   constexpr int MP = Cfg::kMP;
@@ -347,8 +355,12 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     float sum = 0.0f;
     for (int r = 0; r < ks; ++r) sum += ld_dsmem_f32(red + row * MP + m, static_cast<uint32_t>(r));
     const int n = nb * kChunkRows + row;
-    if (n < N) C[static_cast<size_t>(m) * N + n] = gv_out<OutT>(sum);
+    if (n < N) {
+      const OutT v = gv_out<OutT>(sum);
+      for (int d = 0; d < out.count; ++d) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
+    }
   }
+  if (out.fence_sys) __threadfence_system();
   cluster_sync_all();
 }
 

@@ -82,12 +82,34 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const vo
   return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
 }
 
+// 2-D map over rows of `inner` elements spaced `row_bytes` apart (a column slice of a wider
+// row-major matrix), no swizzle.
+int encode_2d_strided(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
+                      uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return MXFP4_ERR_DRIVER;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
+}
+
 inline int k_blocks_of(int K) { return ceil_div(K, kChunkK); }
 inline int n_blocks_of(int N) { return ceil_div(N, kChunkRows); }
 
+// Where a GEMM's [M, N] result goes: dst[i] + (m * ldc + n_off + n) elements, i < count.
+struct OutSpec {
+  void* const* dst;
+  int count, ldc, n_off, fence_sys;
+};
+
 // ------------------------------------------------------------------ large-M launch
 template <bool kTS, typename OutT>
-int launch_tc(const void* A, const uint8_t* wpack, void* C, int M, int N, int K, cudaStream_t stream,
+int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int N, int K, cudaStream_t stream,
               DeviceState* d) {
   using Cfg = TcCfg<kTS, OutT>;
   const int slot = (kTS ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
@@ -97,19 +119,26 @@ int launch_tc(const void* A, const uint8_t* wpack, void* C, int M, int N, int K,
     if (e != cudaSuccess) return ret(e);
     d->tc_attr[slot] = true;
   }
-  CUtensorMap tm_act, tm_out;
+  CUtensorMap tm_act;
+  TcOut out;
+  std::memset(&out, 0, sizeof(out));
   int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, kTcBK, kTcTileAct,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d(&tm_out,
-                 sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                 static_cast<int>(sizeof(OutT)), C, N, M, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
+  for (int i = 0; i < o.count; ++i) {
+    rc = encode_2d_strided(&out.map[i],
+                           sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           static_cast<int>(sizeof(OutT)), static_cast<OutT*>(o.dst[i]) + o.n_off, N, M,
+                           static_cast<uint64_t>(o.ldc) * sizeof(OutT), 32, 32);
+    if (rc) return rc;
+  }
+  out.count = o.count;
+  out.fence_sys = o.fence_sys;
   const int m_blocks = ceil_div(M, kTcTileAct);
   const int n_blocks = n_blocks_of(N);
   const int tiles = m_blocks * n_blocks;
   const int grid = std::min(tiles, d->sm_count);
-  gemm_tc_kernel<kTS, OutT><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(tm_act, tm_out, wpack, M,
+  gemm_tc_kernel<kTS, OutT><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(tm_act, out, wpack, M,
                                                                            k_blocks_of(K), m_blocks, n_blocks);
   return launch_status();
 }
@@ -145,8 +174,15 @@ GvPlan plan_gemv(int M, int N, int K, int sm_count) {
 }
 
 template <int NT, typename OutT>
-int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, int K, const GvPlan& p,
+int launch_gemv_t(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int N, int K, const GvPlan& p,
                   cudaStream_t stream, DeviceState* d, const uint8_t* xpre, const int* xpre_shift) {
+  GvOut<OutT> out;
+  std::memset(&out, 0, sizeof(out));
+  for (int i = 0; i < o.count; ++i) out.p[i] = static_cast<OutT*>(o.dst[i]);
+  out.count = o.count;
+  out.ldc = o.ldc;
+  out.n_off = o.n_off;
+  out.fence_sys = o.fence_sys;
   const int slot = (NT == 1 ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
   if (!d->gv_attr[slot]) {
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -171,7 +207,7 @@ int launch_gemv_t(const void* A, const uint8_t* wpack, void* C, int M, int N, in
   cfg.attrs = attr;
   cfg.numAttrs = xpre ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, OutT>, static_cast<const __nv_bfloat16*>(A), M, K,
-                                     wpack, k_blocks_of(K), p.kbps, p.stages, static_cast<OutT*>(C), N,
+                                     wpack, k_blocks_of(K), p.kbps, p.stages, out, N,
                                      xpre, xpre_shift);
   return ret(e);
 }
@@ -186,7 +222,7 @@ size_t gemv_prestage_bytes(int M, int N, int K) {
   return static_cast<size_t>(k_blocks_of(K)) * 128 * M + 256;
 }
 
-int launch_gemv(const void* A, const uint8_t* wpack, void* C, int c_dtype, int M, int N, int K,
+int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
                 cudaStream_t stream, DeviceState* d, uint8_t* xws, size_t xws_bytes) {
   const GvPlan p = plan_gemv(M, N, K, d->sm_count);
   if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
@@ -383,16 +419,26 @@ size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
   return pre + x;
 }
 
-int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype, int M, int N,
-               int K, int layout, int path, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+}  // extern "C"
+
+namespace {
+int gemm_impl(const void* A, const uint8_t* B, const uint8_t* B_scales, const OutSpec& C, int c_dtype, int M, int N,
+              int K, int layout, int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!A || !B || M <= 0 || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (C.count < 1 || C.count > kMaxOutDst || C.n_off < 0 || C.ldc < C.n_off + N) return MXFP4_ERR_INVALID_ARGUMENT;
+  const size_t esz = c_dtype == MXFP4_DTYPE_F32 ? 4 : 2;
+  for (int i = 0; i < C.count; ++i) {
+    if (!C.dst[i]) return MXFP4_ERR_INVALID_ARGUMENT;
+    if (!aligned16(static_cast<const char*>(C.dst[i]) + C.n_off * esz) || (C.ldc * esz) % 16)
+      return MXFP4_ERR_MISALIGNED;
+  }
   if (c_dtype != MXFP4_DTYPE_F32 && c_dtype != MXFP4_DTYPE_BF16) return MXFP4_ERR_INVALID_ARGUMENT;
   if (layout < MXFP4_LAYOUT_REF || layout > MXFP4_LAYOUT_PREPACKED) return MXFP4_ERR_INVALID_ARGUMENT;
   if (path < MXFP4_PATH_AUTO || path > MXFP4_PATH_GEMV) return MXFP4_ERR_INVALID_ARGUMENT;
   if (layout != MXFP4_LAYOUT_PREPACKED && !B_scales) return MXFP4_ERR_INVALID_ARGUMENT;
   if (path == MXFP4_PATH_AUTO) path = mxfp4_select_path(M, N, K);
   if (!mxfp4_shape_supported(path, M, N, K)) return MXFP4_ERR_UNSUPPORTED_SHAPE;
-  if (!aligned16(A) || !aligned16(C) || !aligned16(B)) return MXFP4_ERR_MISALIGNED;
+  if (!aligned16(A) || !aligned16(B)) return MXFP4_ERR_MISALIGNED;
   DeviceState* d = nullptr;
   int rc = current_device(&d);
   if (rc) return rc;
@@ -423,6 +469,68 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
     default: return MXFP4_ERR_INVALID_ARGUMENT;
   }
 }
+}  // namespace
+
+extern "C" {
+
+int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype, int M, int N,
+               int K, int layout, int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!C) return MXFP4_ERR_INVALID_ARGUMENT;
+  void* dst[1] = {C};
+  const OutSpec o{dst, 1, N, 0, 0};
+  return gemm_impl(A, B, B_scales, o, c_dtype, M, N, K, layout, path, workspace, workspace_bytes, stream);
+}
+
+int mxfp4_gemm_allgather(const void* A, const uint8_t* B_prepacked, void* const* C_dst, int n_dst, int n_off,
+                         int ldc, int c_dtype, int M, int N, int K, int path, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (!C_dst || n_dst < 1 || n_dst > kMaxOutDst) return MXFP4_ERR_INVALID_ARGUMENT;
+  const OutSpec o{C_dst, n_dst, ldc, n_off, 1};
+  return gemm_impl(A, B_prepacked, nullptr, o, c_dtype, M, N, K, MXFP4_LAYOUT_PREPACKED, path, workspace,
+                   workspace_bytes, stream);
+}
+
+size_t mxfp4_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int mxfp4_ipc_export(const void* dev_ptr, void* handle_out, size_t* offset_out) {
+  if (!dev_ptr || !handle_out || !offset_out) return MXFP4_ERR_INVALID_ARGUMENT;
+  static PFN_cuMemGetAddressRange_v3020 range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+  });
+  if (!range_fn) return MXFP4_ERR_DRIVER;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return MXFP4_ERR_DRIVER;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return ret(e);
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = reinterpret_cast<uintptr_t>(dev_ptr) - static_cast<uintptr_t>(base);
+  return 0;
+}
+
+int mxfp4_ipc_open(const void* handle, size_t offset, void** dev_ptr_out) {
+  if (!handle || !dev_ptr_out) return MXFP4_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return ret(e);
+  *dev_ptr_out = static_cast<char*>(base) + offset;
+  return 0;
+}
+
+int mxfp4_ipc_close(void* dev_ptr, size_t offset) {
+  if (!dev_ptr) return MXFP4_ERR_INVALID_ARGUMENT;
+  return ret(cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset));
+}
+
 
 }  // extern "C"
 

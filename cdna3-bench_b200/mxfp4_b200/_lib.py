@@ -37,6 +37,11 @@ EXPORTED = (
     "mxfp4_gemm_workspace_bytes",
     "mxfp4_gemm",
     "mxfp4_gemm_noalloc",
+    "mxfp4_gemm_allgather",
+    "mxfp4_ipc_handle_bytes",
+    "mxfp4_ipc_export",
+    "mxfp4_ipc_open",
+    "mxfp4_ipc_close",
 )
 
 
@@ -81,6 +86,11 @@ def _declare(lib):
         "mxfp4_gemm_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
         "mxfp4_gemm": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
         "mxfp4_gemm_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+        "mxfp4_gemm_allgather": (_I, [_P, _P, ctypes.POINTER(_P), _I, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+        "mxfp4_ipc_handle_bytes": (_SZ, []),
+        "mxfp4_ipc_export": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
+        "mxfp4_ipc_open": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
+        "mxfp4_ipc_close": (_I, [_P, _SZ]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -230,6 +230,45 @@ def gemm(A: torch.Tensor, w: MXFP4Weight, out_dtype=torch.bfloat16, path: str = 
     return C
 
 
+def gemm_allgather(A: torch.Tensor, w: MXFP4Weight, dst_ptrs, n_off: int, ldc: int,
+                   out_dtype=torch.bfloat16, path: str = "auto"):
+    """This GPU's columns of C = A @ dequant(w)^T, written straight into every buffer in
+    `dst_ptrs` (device addresses of the [M, ldc] outputs of all GPUs, peers' opened with
+    :func:`ipc_open`) at columns n_off .. n_off + w.N - 1.  Returns nothing; the caller orders
+    later reads of the peers' writes (a collective on the same stream on every GPU)."""
+    _check_A(A, w.K)
+    M = A.shape[0]
+    L = _lib.lib()
+    arr = (ctypes.c_void_p * len(dst_ptrs))(*[int(p) for p in dst_ptrs])
+    nws = L.mxfp4_gemm_workspace_bytes(M, w.N, w.K, _lib.LAYOUT_PREPACKED)
+    ws = torch.empty(nws, dtype=torch.uint8, device=A.device) if nws else None
+    _lib.check(
+        L.mxfp4_gemm_allgather(_ptr(A), _ptr(w.data), arr, len(dst_ptrs), n_off, ldc, _ODT[out_dtype], M, w.N, w.K,
+                               _lib.PATH_NAMES[path], _ptr(ws) if ws is not None else None, nws, _stream()),
+        "mxfp4_gemm_allgather",
+    )
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(handle, offset) through which another process on this node maps `t`'s memory."""
+    L = _lib.lib()
+    h = ctypes.create_string_buffer(L.mxfp4_ipc_handle_bytes())
+    off = ctypes.c_size_t(0)
+    _lib.check(L.mxfp4_ipc_export(_ptr(t), h, ctypes.byref(off)), "mxfp4_ipc_export")
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """Device address, in this process, of memory another process exported."""
+    p = ctypes.c_void_p(0)
+    _lib.check(_lib.lib().mxfp4_ipc_open(handle, offset, ctypes.byref(p)), "mxfp4_ipc_open")
+    return int(p.value)
+
+
+def ipc_close(ptr: int, offset: int) -> None:
+    _lib.check(_lib.lib().mxfp4_ipc_close(ctypes.c_void_p(ptr), offset), "mxfp4_ipc_close")
+
+
 def _gemm_layout(A, B, Bs, C, layout: int, N: int, K: int, path: int, name: str):
     M = A.shape[0]
     if C is None:

@@ -97,3 +97,61 @@ class ColumnParallelMXFP4:
     def forward(self, A: torch.Tensor, gather: bool = True, group=None, out_dtype=torch.bfloat16):
         Y = self.local(A, out_dtype)
         return all_gather_columns(Y, self.N, group) if gather and self.world > 1 else Y
+
+
+class PeerOutput:
+    """A full [M, N] output buffer on every GPU of the group, each mapped into every other
+    process (CUDA IPC), so that a fused GEMM + all-gather can store its tiles straight into
+    all of them over NVLink.  Collective: every rank constructs it with the same arguments."""
+
+    def __init__(self, M: int, N: int, dtype=torch.bfloat16, group=None, device=None):
+        import torch.distributed as dist
+
+        from . import kernels as kk
+
+        self.M, self.N, self.dtype, self.group = M, N, dtype, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the fused all-gather writes to at most 8 GPUs")
+        self.buffer = torch.empty((M, N), dtype=dtype, device=device or torch.cuda.current_device())
+        handle, off = kk.ipc_export(self.buffer)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (handle, off), group=group)
+        self._opened = []
+        self.ptrs = []
+        for r, (h, o) in enumerate(everyone):
+            if r == self.rank:
+                self.ptrs.append(self.buffer.data_ptr())
+            else:
+                p = kk.ipc_open(h, o)
+                self._opened.append((p, o))
+                self.ptrs.append(p)
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.buffer.device)
+
+    def close(self):
+        from . import kernels as kk
+
+        for p, o in self._opened:
+            kk.ipc_close(p, o)
+        self._opened = []
+
+    def sync(self):
+        """Order this GPU's later work after every peer's stores into `buffer` (a stream-ordered
+        all-reduce of one int: it completes only after every rank's preceding kernels)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._flag, group=self.group)
+
+
+def forward_fused(layer: "ColumnParallelMXFP4", A: torch.Tensor, out: PeerOutput) -> torch.Tensor:
+    """Column-parallel GEMM with the all-gather fused into the epilogue: every output tile is
+    stored into all GPUs' `out.buffer` as it is produced, then one tiny collective orders the
+    reads.  Returns this GPU's full [M, N] output."""
+    from . import kernels as kk
+
+    if out.dtype not in (torch.bfloat16, torch.float32) or out.N != layer.N or out.M != A.shape[0]:
+        raise ValueError("PeerOutput shape/dtype does not match the layer and A")
+    kk.gemm_allgather(A, layer.weight, out.ptrs, layer.n0, layer.N, out_dtype=out.dtype)
+    out.sync()
+    return out.buffer

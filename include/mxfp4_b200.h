@@ -135,6 +135,29 @@ int mxfp4_gemm(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C
                int M, int N, int K, int layout, int path, void* workspace, size_t workspace_bytes,
                void* stream);
 
+/* Column-parallel GEMM with the all-gather fused into the epilogue.  Replaces the reference
+ * pair "gemm_X on this rank's weight columns" + a separate all-gather of the outputs (the
+ * multi-GPU sharding the reference leaves to its callers; no single reference function).
+ * B_prepacked: this GPU's column slice of the weights (N columns), PREPACKED layout.  The
+ * [M, N] result is written, as the tiles are produced, into each of the n_dst (<= 8) buffers
+ * C_dst[i] -- every GPU's full [M, ldc] output, this GPU's own and its peers' (opened with
+ * mxfp4_ipc_open) -- at columns n_off .. n_off+N-1.  The stores are made visible system-wide
+ * before the kernel ends; the caller still orders the peers' later reads after this kernel
+ * (e.g. a stream-ordered collective on the same stream on every GPU).  Workspace as for
+ * mxfp4_gemm with the PREPACKED layout. */
+int mxfp4_gemm_allgather(const void* A, const uint8_t* B_prepacked, void* const* C_dst, int n_dst, int n_off,
+                         int ldc, int c_dtype, int M, int N, int K, int path, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* CUDA IPC for the all-gather destinations (no reference counterpart: the reference runs on
+ * one GPU).  mxfp4_ipc_export gives the handle (mxfp4_ipc_handle_bytes() bytes) of the
+ * allocation holding dev_ptr and dev_ptr's offset in it; another process on the same node
+ * maps it with mxfp4_ipc_open and unmaps it with mxfp4_ipc_close (same offset). */
+size_t mxfp4_ipc_handle_bytes(void);
+int mxfp4_ipc_export(const void* dev_ptr, void* handle_out, size_t* offset_out);
+int mxfp4_ipc_open(const void* handle, size_t offset, void** dev_ptr_out);
+int mxfp4_ipc_close(void* dev_ptr, size_t offset);
+
 /* Fixed size of the device buffer mxfp4_gemm_noalloc uses in place of a workspace. */
 #define MXFP4_NOALLOC_SCRATCH_BYTES (32u << 20)
 

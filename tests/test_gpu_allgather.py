@@ -1,0 +1,89 @@
+"""The fused column-parallel GEMM + all-gather (mxfp4_gemm_allgather): every destination
+receives this GPU's columns at the right offset, for both kernel families; on two GPUs the
+gathered output equals the unsharded product."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import mxfp4_ref as o
+from _util import make_case, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,path", [(256, "tc"), (300, "tc_smem"), (4, "gemv"), (16, "gemv")])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_multi_destination_single_gpu(M, path, dtype):
+    """Three local buffers stand in for three GPUs' outputs: each gets the slice at n_off."""
+    import mxfp4_b200 as mx
+    from mxfp4_b200 import kernels as kk
+
+    N, K, ldc, n_off = 384, 512, 1024, 512
+    A, Bp, Bs = make_case(M, N, K, seed=3 + M)
+    ref = o.ref_gemm(A, Bp, Bs)
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).cuda().to(torch.bfloat16)
+    bufs = [torch.full((M, ldc), 7.0, dtype=dtype, device="cuda") for _ in range(3)]
+    kk.gemm_allgather(At, w, [b.data_ptr() for b in bufs], n_off, ldc, out_dtype=dtype, path=path)
+    torch.cuda.synchronize()
+    assert mx.device_error() == 0
+    for b in bufs:
+        h = b.float().cpu().numpy()
+        assert rel_err(h[:, n_off:n_off + N], ref) <= 1e-2
+        assert (h[:, :n_off] == 7.0).all() and (h[:, n_off + N:] == 7.0).all()  # nothing outside the slice
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from mxfp4_b200 import sharding
+
+        res = {}
+        for M in (512, 8):
+            N, K = 1024, 768
+            A, Bp, Bs = make_case(M, N, K, seed=21 + M)
+            layer = sharding.ColumnParallelMXFP4(torch.from_numpy(Bp).cuda(), torch.from_numpy(Bs).cuda(), N, world, rank)
+            out = sharding.PeerOutput(M, N, torch.float32)
+            At = torch.from_numpy(A).cuda().to(torch.bfloat16)
+            for _ in range(2):  # twice: the buffer is reused
+                Y = sharding.forward_fused(layer, At, out)
+            torch.cuda.synchronize()
+            res[M] = rel_err(Y.cpu().numpy(), o.ref_gemm(A, Bp, Bs))
+            dist.barrier()
+            out.close()
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_fused_allgather_equals_unsharded():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        for M, err in got[r].items():
+            assert err <= 1e-2, (r, M, err)
