@@ -237,23 +237,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);  // accumulator free: the next tile's MMAs start
+        if (out.count == 1) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {  // four 32-row slabs
-          const int mc = m0 + 32 * c;
-          if (!(MXFP4_TC_DIAG & 8) && mc < M) {
-            if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
-            __syncwarp();
+          for (int c = 0; c < 4; ++c) {  // four 32-row slabs
+            const int mc = m0 + 32 * c;
+            if (!(MXFP4_TC_DIAG & 8) && mc < M) {
+              if (lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
+              __syncwarp();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint32_t pk = packed[16 * c + j];
-              sts16(stage + ((2 * j) * 32 + lane) * 2, pk & 0xFFFFu);
-              sts16(stage + ((2 * j + 1) * 32 + lane) * 2, pk >> 16);
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t pk = packed[16 * c + j];
+                sts16(stage + ((2 * j) * 32 + lane) * 2, pk & 0xFFFFu);
+                sts16(stage + ((2 * j + 1) * 32 + lane) * 2, pk >> 16);
+              }
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&out.map[0], stage_ptr, n0, mc);
+                bulk_commit();
+              }
             }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage_ptr, n0, mc);
-              bulk_commit();
+          }
+        } else {
+          // bf16: the two warps of adjacent column quarters (ew, ew^1) fill one 32-row x 64-column
+          // slab (128-byte rows, the unit that crosses NVLink efficiently when a destination is a
+          // peer's buffer) and the even warp stores it.
+          const int pair = ew >> 1, half = ew & 1;
+          uint8_t* pair_ptr = smem + Cfg::kOffOut + pair * 2 * Cfg::kSlabBytes;
+          const uint32_t pstage = smem_u32(pair_ptr);
+          const int n_pair = n0 - 32 * half;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {  // four 32-row slabs
+            const int mc = m0 + 32 * c;
+            if (!(MXFP4_TC_DIAG & 8) && mc < M) {
+              if (half == 0 && lane == 0) bulk_wait_read<0>();  // the previous store has read the buffer
+              named_bar_sync(2 + pair, 64);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t pk = packed[16 * c + j];
+                sts16(pstage + ((2 * j) * 64 + 32 * half + lane) * 2, pk & 0xFFFFu);
+                sts16(pstage + ((2 * j + 1) * 64 + 32 * half + lane) * 2, pk >> 16);
+              }
+              fence_proxy_async_smem();
+              named_bar_sync(2 + pair, 64);
+              if (half == 0 && lane == 0) {
+                for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], pair_ptr, n_pair, mc);
+                bulk_commit();
+              }
             }
           }
         }

@@ -129,7 +129,8 @@ int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int 
     rc = encode_2d_strided(&out.map[i],
                            sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            static_cast<int>(sizeof(OutT)), static_cast<OutT*>(o.dst[i]) + o.n_off, N, M,
-                           static_cast<uint64_t>(o.ldc) * sizeof(OutT), 32, 32);
+                           static_cast<uint64_t>(o.ldc) * sizeof(OutT),
+                           sizeof(OutT) == 2 && o.count > 1 ? 64 : 32, 32);  // paired bf16 slabs
     if (rc) return rc;
   }
   out.count = o.count;
