@@ -397,6 +397,16 @@ def main():
                 "kernel": "gemm_tc_kernel",
                 "peak_source": f"{peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16"}
     roof["traffic"] = load_traffic(args.workload)
+    if fused is not None:  # the fused GEMM + all-gather: compute or NVLink, whichever is slower
+        link_gbs = 770.0  # measured peer copy per direction on this pool's B200s
+        sent = sum(M * it["N"] * 2 * (world - 1) for it in items)
+        t_link = sent / (link_gbs * 1e9)
+        t_comp = flops_step / (peaks.bf16_tflops_sustained * 1e12)
+        if t_link > t_comp:
+            ach = sent / (sum(launch_ms) * 1e-3) / 1e9
+            roof = {"bound": "nvlink", "achieved": ach, "peak": link_gbs, "unit": "GB/s", "frac": ach / link_gbs,
+                    "kernel": "gemm_tc_kernel (all-gather epilogue)",
+                    "peak_source": "measured NVLink peer copy per direction", "traffic": None}
 
     e2e = None
     if not args.no_e2e and args.workload != "tp_sweep":
