@@ -74,7 +74,7 @@ def parse():
                     help="column-parallel: GEMM then a separate NCCL all-gather (default: all-gather fused "
                          "into the GEMM epilogue, stores straight into every GPU's output over NVLink)")
     ap.add_argument("--no-graph", action="store_true",
-                    help="decode workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
+                    help="decode and c0 workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
     return ap.parse_args()
 
 
@@ -283,9 +283,11 @@ def main():
     bytes_step = sum(cost_model.Shape(M, it["N"], it["K"]).in_bytes for it in items)
     units_step = bytes_step if decode else flops_step
 
-    # decode weights fit in L2: rotate copies so the bytes between two reads of one copy exceed L2
+    # decode and c0 weights fit in L2: rotate copies so the bytes between two reads of one copy
+    # exceed L2 (c0's activations, 0.8 MB, stay resident as they would in a serving loop)
+    small = decode or args.workload == "c0"
     rot = 1
-    if decode:
+    if small:
         l2 = torch.cuda.get_device_properties(dev).L2_cache_size
         rot = max(1, -(-3 * l2 // bytes_step))
         for it in items:
@@ -312,7 +314,7 @@ def main():
 
     def step(i_step: int, record: bool):
         for j, it in enumerate(items):
-            w = it["w_rot"][i_step % rot] if decode else it["w"]
+            w = it["w_rot"][i_step % rot] if small else it["w"]
             if record:
                 ev[i_step][j][0].record()
             if fused is not None:
@@ -330,11 +332,11 @@ def main():
         step(i, False)
     barrier()
 
-    # Decode GEMMs last ~10-60 us, about the host cost of a Python launch: a serving loop
+    # Decode and c0 GEMMs last ~5-60 us, about the host cost of a Python launch: a serving loop
     # replays them from a CUDA graph, and so does the bench (one graph per weight rotation,
     # with timing events recorded as graph nodes around every GEMM).
     graphs = None
-    if decode and not args.no_graph and gather is None:
+    if small and not args.no_graph and gather is None:
         graphs, gev = [], []
         for r in range(rot):
             evs = [(torch.cuda.Event(enable_timing=True, external=True),
@@ -432,7 +434,7 @@ def main():
                 "gemms": [[it["name"], it["N"], it["K"]] for it in items],
                 "weights": "MXFP4 (E2M1 + E8M0/32), prepacked, resident in HBM",
                 "output": "bf16", "accumulate": "fp32",
-                "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if decode
+                "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if small
                        else "inputs larger than L2: one step touches "
                             f"{(bytes_step + sum(M * it['N'] * 2 for it in items)) / 1e6:.0f} MB"),
                 "launch": "one CUDA graph per step" if graphs is not None else "eager, one launch per GEMM",

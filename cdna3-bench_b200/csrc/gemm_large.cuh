@@ -18,7 +18,9 @@
 //     bf16) and hand the accumulator back to the MMA issuer BEFORE storing, so the next
 //     tile's MMAs overlap the stores; each warp then writes 32 x 32 slabs through its own
 //     smem staging buffer with TMA tensor stores.
-//   * Persistent CTAs (one per SM) walk the tile list in a grouped raster order.
+//   * Persistent CTAs (one per SM) walk the tile list in a grouped raster order.  When there are
+//     too few tiles to fill the GPU (small M x N), K is split too: each tile slice stores an
+//     fp32 partial through a 3-D map into workspace and splitk_reduce_kernel sums them.
 //
 // Warp roles (576 threads): 0 = TMA producer, 1 = MMA issuer (+TMEM owner),
 // 2..9 = epilogue, 10..17 = dequant (two per TMEM lane quarter, one per 32-element half of
@@ -75,6 +77,16 @@ __device__ __forceinline__ void tc_tile_coords(int t, int m_blocks, int n_blocks
   nb = local / gm;
 }
 
+// Tile t of the persistent schedule: split-K slice ks (outermost), then the grouped raster.
+__device__ __forceinline__ void tc_tile(int t, int m_blocks, int n_blocks, int k_blocks, int kbps, int& mb,
+                                        int& nb, int& kb_lo, int& kb_hi, int& ks) {
+  const int mn = m_blocks * n_blocks;
+  ks = t / mn;
+  tc_tile_coords(t - ks * mn, m_blocks, n_blocks, mb, nb);
+  kb_lo = ks * kbps;
+  kb_hi = min(k_blocks, kb_lo + kbps);
+}
+
 // Output destinations: the epilogue stores every output slab through each of these maps.  One
 // map is the plain GEMM; several give the all-gather form, where each map covers this GPU's
 // column slice of one GPU's full output buffer (its own, or a peer's over NVLink).
@@ -83,12 +95,14 @@ struct TcOut {
   CUtensorMap map[kMaxOutDst];
   int count;
   int fence_sys;  // 1: make the stores visible system-wide before the kernel ends (peer buffers)
+  int split3d;    // 1: map[0] is a 3-D fp32 map over split-K partials [splits][M][N]
 };
 
 template <bool kTS, typename OutT>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ TcOut out,
-                   const uint8_t* __restrict__ wpack, int M, int k_blocks, int m_blocks, int n_blocks) {
+                   const uint8_t* __restrict__ wpack, int M, int k_blocks, int m_blocks, int n_blocks,
+                   int k_splits, int kbps) {
   using Cfg = TcCfg<kTS, OutT>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -103,7 +117,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int total = m_blocks * n_blocks;
+  const int total = m_blocks * n_blocks * k_splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -134,10 +148,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t ph = 0, pend = 0, pend_ph = 0;
       bool aborted = false;
       for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
-        int mb, nb;
-        tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
+        int mb, nb, kb_lo, kb_hi, ks;
+        tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
         const uint8_t* wsrc = wpack + static_cast<size_t>(nb) * k_blocks * kChunkBytes;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
             aborted = true;
             break;
@@ -172,7 +186,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         tc_fence_after();
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        int mb, nb, kb_lo, kb_hi, ks;
+        tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[s], ph, kErrWaitFull, abort_flag) ||
               !mbar_wait(&dqd[s], ph, kErrWaitDequant, abort_flag)) {
             aborted = true;
@@ -183,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             if (MXFP4_TC_DIAG & 4) break;
-            const uint32_t acc = (kb | i) != 0;
+            const uint32_t acc = ((kb - kb_lo) | i) != 0;
             if constexpr (kTS) {
               mma_ts(tmem + kTmemAccCol, tmem + kTmemARingCol + s * 32 + i * 8, bdesc + 2 * i, idesc, acc);
             } else {
@@ -216,8 +232,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t stage = smem_u32(stage_ptr);
     uint32_t aph = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      int mb, nb;
-      tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
+      int mb, nb, kb_lo, kb_hi, ks;
+      tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
       if (!warp_wait(acc_full, aph, kErrWaitAccFull, abort_flag)) break;
       tc_fence_after();
       const int m0 = mb * kTcTileAct + 128 * hh;  // activation rows m0 .. m0+127 of this warp
@@ -307,7 +323,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage_ptr, n0, mc);
+              if (out.split3d)
+                tma_store_3d(&out.map[0], stage_ptr, n0, mc, ks);
+              else
+                for (int d = 0; d < out.count; ++d) tma_store_2d(&out.map[d], stage_ptr, n0, mc);
               bulk_commit();
             }
           }
@@ -329,7 +348,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t ph = 0;
     bool aborted = false;
     for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
-      for (int kb = 0; kb < k_blocks; ++kb) {
+      int mb, nb, kb_lo, kb_hi, ks;
+      tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
         if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
           aborted = true;
           break;
@@ -373,6 +394,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Sum of the split-K partials ws[splits][M][N] (fp32) into C (row stride ldc).  Four columns
+// per thread; N is a multiple of 4 on this path.
+template <typename OutT>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
+                                                            OutT* __restrict__ C, int ldc) {
+  const size_t n4 = static_cast<size_t>(N) / 4;
+  const size_t total = static_cast<size_t>(M) * n4;
+  const size_t plane = static_cast<size_t>(M) * N;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t m = i / n4, c = (i - m * n4) * 4;
+    float4 acc = *reinterpret_cast<const float4*>(ws + m * N + c);
+    for (int s = 1; s < splits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + s * plane + m * N + c);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    OutT* dst = C + m * ldc + c;
+    if constexpr (sizeof(OutT) == 4) {
+      *reinterpret_cast<float4*>(dst) = acc;
+    } else {
+      const uint32_t lo = pack_bf16x2(acc.x, acc.y), hi = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+    }
   }
 }
 

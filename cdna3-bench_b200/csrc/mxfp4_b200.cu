@@ -108,9 +108,43 @@ struct OutSpec {
 };
 
 // ------------------------------------------------------------------ large-M launch
+// Split-K plan of the large-M kernel: with fewer tiles than half the SMs, K is split so that
+// ~all SMs work (at most 8 slices, each at least 8 K-blocks).  1 = no split.
+struct SplitPlan {
+  int splits, kbps;
+};
+SplitPlan plan_splitk(int M, int N, int K, int sm_count) {
+  const int tiles = ceil_div(M, kTcTileAct) * n_blocks_of(N);
+  const int kb = k_blocks_of(K);
+  SplitPlan p{1, kb};
+  if (2 * tiles > sm_count || N % 4) return p;
+  int s = std::min({8, sm_count / tiles, kb / 8});
+  if (s < 2) return p;
+  p.kbps = ceil_div(kb, s);
+  p.splits = ceil_div(kb, p.kbps);  // no empty slice
+  return p;
+}
+size_t splitk_bytes(int M, int N, int K, int sm_count) {
+  const SplitPlan p = plan_splitk(M, N, K, sm_count);
+  return p.splits > 1 ? static_cast<size_t>(p.splits) * M * N * 4 : 0;
+}
+
+int encode_3d_f32(CUtensorMap* map, const float* base, uint64_t n, uint64_t m, uint64_t planes) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return MXFP4_ERR_DRIVER;
+  cuuint64_t dims[3] = {n, m, planes};
+  cuuint64_t strides[2] = {n * 4, n * m * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
+}
+
 template <bool kTS, typename OutT>
 int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int N, int K, cudaStream_t stream,
-              DeviceState* d) {
+              DeviceState* d, const SplitPlan& sp = SplitPlan{1, 0}, float* splitws = nullptr) {
   using Cfg = TcCfg<kTS, OutT>;
   const int slot = (kTS ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
   if (!d->tc_attr[slot]) {
@@ -125,7 +159,7 @@ int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int 
   int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, A, K, M, kTcBK, kTcTileAct,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  for (int i = 0; i < o.count; ++i) {
+  for (int i = 0; i < (sp.splits > 1 ? 0 : o.count); ++i) {
     rc = encode_2d_strided(&out.map[i],
                            sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            static_cast<int>(sizeof(OutT)), static_cast<OutT*>(o.dst[i]) + o.n_off, N, M,
@@ -135,12 +169,35 @@ int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int 
   }
   out.count = o.count;
   out.fence_sys = o.fence_sys;
+  if (sp.splits > 1) {  // fp32 partials [splits][M][N] into the workspace (OutT is float here)
+    rc = encode_3d_f32(&out.map[0], splitws, N, M, sp.splits);
+    if (rc) return rc;
+    out.count = 1;
+    out.split3d = 1;
+  }
   const int m_blocks = ceil_div(M, kTcTileAct);
   const int n_blocks = n_blocks_of(N);
-  const int tiles = m_blocks * n_blocks;
+  const int tiles = m_blocks * n_blocks * sp.splits;
   const int grid = std::min(tiles, d->sm_count);
-  gemm_tc_kernel<kTS, OutT><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(tm_act, out, wpack, M,
-                                                                           k_blocks_of(K), m_blocks, n_blocks);
+  gemm_tc_kernel<kTS, OutT><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(
+      tm_act, out, wpack, M, k_blocks_of(K), m_blocks, n_blocks, sp.splits, sp.splits > 1 ? sp.kbps : k_blocks_of(K));
+  return launch_status();
+}
+
+// Large-M kernel with split-K: fp32 partials into `ws`, then one reduction into C.
+template <bool kTS>
+int launch_tc_splitk(const void* A, const uint8_t* wpack, const OutSpec& o, int c_dtype, int M, int N, int K,
+                     const SplitPlan& sp, float* ws, cudaStream_t stream, DeviceState* d) {
+  int rc = launch_tc<kTS, float>(A, wpack, o, M, N, K, stream, d, sp, ws);
+  if (rc) return rc;
+  const size_t work = static_cast<size_t>(M) * (N / 4);
+  const int blocks = static_cast<int>(std::min<size_t>(ceil_div(static_cast<int>(std::min<size_t>(work, 1u << 30)), 256),
+                                                       static_cast<size_t>(d->sm_count) * 8));
+  if (c_dtype == MXFP4_DTYPE_F32)
+    splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N, static_cast<float*>(o.dst[0]), o.ldc);
+  else
+    splitk_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N,
+                                                                    static_cast<__nv_bfloat16*>(o.dst[0]), o.ldc);
   return launch_status();
 }
 
@@ -417,7 +474,9 @@ size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const size_t pre = layout == MXFP4_LAYOUT_PREPACKED ? 0 : (prepacked_bytes(N, K) + 255) / 256 * 256;
   const size_t x = gemv_prestage_bytes(M, N, K);  // M <= 16: the decode path may serve the call
-  return pre + x;
+  DeviceState* d = nullptr;
+  const size_t sk = M > 16 && current_device(&d) == 0 ? splitk_bytes(M, N, K, d->sm_count) : 0;
+  return pre + std::max(x, sk);
 }
 
 }  // extern "C"
@@ -458,6 +517,21 @@ int gemm_impl(const void* A, const uint8_t* B, const uint8_t* B_scales, const Ou
     const size_t used = (need + 255) / 256 * 256;
     rest = workspace_bytes > used ? static_cast<uint8_t*>(workspace) + used : nullptr;
     rest_bytes = workspace_bytes > used ? workspace_bytes - used : 0;
+  }
+  switch (path) {
+    case MXFP4_PATH_TC:
+    case MXFP4_PATH_TC_SMEM: {
+      const SplitPlan sp = plan_splitk(M, N, K, d->sm_count);
+      const size_t need = static_cast<size_t>(sp.splits) * M * N * 4;
+      if (sp.splits > 1 && C.count == 1 && C.n_off == 0 && rest && rest_bytes >= need && aligned16(rest)) {
+        float* ws = reinterpret_cast<float*>(rest);
+        return path == MXFP4_PATH_TC ? launch_tc_splitk<true>(A, wpack, C, c_dtype, M, N, K, sp, ws, s, d)
+                                     : launch_tc_splitk<false>(A, wpack, C, c_dtype, M, N, K, sp, ws, s, d);
+      }
+      break;
+    }
+    default:
+      break;
   }
   switch (path) {
     case MXFP4_PATH_TC:

@@ -165,3 +165,33 @@ def test_gemv_without_workspace_stages_in_kernel(mx, M):
         outs.append(C.cpu().numpy())
         assert rel_err(outs[-1], ref) <= TOL
     assert mx.workspace_bytes(M, N, K, "prepacked") > 0
+
+
+@pytest.mark.parametrize("path", ["tc", "tc_smem"])
+@pytest.mark.parametrize("M,N,K", [(128, 3072, 3072), (64, 640, 4096), (200, 256, 1024), (300, 1024, 8192)])
+def test_tc_split_k_matches_unsplit(mx, path, M, N, K):
+    """Few tiles (small M x N): with workspace the large-M kernel splits K into fp32 partials
+    and reduces them; without workspace it runs unsplit.  Both meet the bound, fp32 and bf16."""
+    import ctypes
+
+    from mxfp4_b200 import _lib
+
+    A, Bp, Bs = make_case(M, N, K, seed=5 * M + K)
+    ref = o.ref_gemm(A, Bp, Bs)
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).to(torch.bfloat16).cuda()
+    nws = int(mx.workspace_bytes(M, N, K, "prepacked"))
+    assert nws > 0  # these shapes fill fewer than half the SMs: split-K is planned
+    for dtype, code in ((torch.float32, _lib.DTYPE_F32), (torch.bfloat16, _lib.DTYPE_BF16)):
+        for ws_bytes in (0, nws):
+            ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+            C = torch.full((M, N), 3.0, dtype=dtype, device="cuda")
+            rc = _lib.lib().mxfp4_gemm(
+                ctypes.c_void_p(At.data_ptr()), ctypes.c_void_p(w.data.data_ptr()), None,
+                ctypes.c_void_p(C.data_ptr()), code, M, N, K, _lib.LAYOUT_PREPACKED, _lib.PATH_NAMES[path],
+                ctypes.c_void_p(ws.data_ptr()) if ws_bytes else None, ws_bytes,
+                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            assert rc == 0
+            torch.cuda.synchronize()
+            assert mx.device_error() == 0
+            assert rel_err(C.float().cpu().numpy(), ref) <= TOL, (dtype, ws_bytes)
