@@ -23,8 +23,8 @@
 //     fp32 partial through a 3-D map into workspace and splitk_reduce_kernel sums them.
 //
 // Warp roles (576 threads): 0 = TMA producer, 1 = MMA issuer (+TMEM owner),
-// 2..9 = epilogue, 10..17 = dequant (two per TMEM lane quarter, one per 32-element half of
-// the stage).  A warp may touch TMEM lanes 32*(warp%4) .. +31 only.
+// 2..9 = epilogue, 10..17 = dequant (one per TMEM lane quarter in each of two groups that
+// take alternate pipeline stages).  A warp may touch TMEM lanes 32*(warp%4) .. +31 only.
 #pragma once
 
 #include "common.cuh"
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&dqd[s], 8);
+      mbar_init(&dqd[s], 4);  // four dequant warps per stage
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -340,47 +340,67 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ dequant
+    // Two groups of four warps take the pipeline steps in turn (group 0 the even ones, group 1
+    // the odd ones); in its step a warp dequantises both 32-element groups of its 32 rows.  Lane
+    // r reads the four 16-byte units t = 0..3 of its row (each unit holds word t of rows r and
+    // r^8 in both groups; lanes r and r^8 read the same unit, so a warp's loads are 16 distinct
+    // units, free of bank conflicts) and keeps the words of its own row.
     const int q = warp & 3;
-    const int h = (warp - kTcFirstDqWarp) >> 2;  // which 32-element group of the stage
-    const int r = 32 * q + lane;                 // weight row inside the tile == TMEM lane
+    const int grp = (warp - kTcFirstDqWarp) >> 2;
+    const int r = 32 * q + lane;  // weight row inside the tile == TMEM lane
+    const int odd = (r >> 3) & 1;
     const uint32_t wbase = smem_u32(smem + Cfg::kOffW);
+    const uint32_t unit0 = (32 * (r >> 4) + 4 * (r & 7)) * 16;
     int s = 0;
-    uint32_t ph = 0;
+    uint32_t ph = 0, it = 0;
     bool aborted = false;
     for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
       int mb, nb, kb_lo, kb_hi, ks;
       tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
-      for (int kb = kb_lo; kb < kb_hi; ++kb) {
-        if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
-          aborted = true;
-          break;
-        }
-        const uint32_t wst = wbase + s * kChunkBytes;
-        uint32_t v[16];
-        if (MXFP4_TC_DIAG & 1) {
+      for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        if ((it & 1) == static_cast<uint32_t>(grp)) {
+          if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
+            aborted = true;
+            break;
+          }
+          const uint32_t wst = wbase + s * kChunkBytes;
+          uint32_t v0[16], v1[16];
+          if (MXFP4_TC_DIAG & 1) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0;
-        } else {
-          const uint4 d = make_uint4(lds32(wst + chunk_word_off(r, h, 0)), lds32(wst + chunk_word_off(r, h, 1)),
-                                     lds32(wst + chunk_word_off(r, h, 2)), lds32(wst + chunk_word_off(r, h, 3)));
-          dequant_rowgroup(d, lds_u8(wst + chunk_scale_off(r, h)), v);
-        }
-        if (MXFP4_TC_DIAG & 2) {
-        } else if constexpr (kTS) {
-          tc_fence_after();
-          tmem_st16(tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemARingCol + s * 32 + h * 16, v);
-          tmem_wait_st();
-          tc_fence_before();
-        } else {
-          const uint32_t at = smem_u32(smem + Cfg::kOffA + s * Cfg::kATileBytes) + r * 128;
+            for (int i = 0; i < 16; ++i) v0[i] = v1[i] = 0;
+          } else {
+            uint32_t w0[4], w1[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            sts128(at + (((4 * h + j) ^ (r & 7)) << 4),
-                   make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-          fence_proxy_async_smem();
+            for (int tt = 0; tt < 4; ++tt) {
+              const uint4 u = lds128(wst + unit0 + tt * 16);
+              w0[tt] = odd ? u.y : u.x;  // (row, group 0)
+              w1[tt] = odd ? u.w : u.z;  // (row, group 1)
+            }
+            const uint32_t sc = lds32(wst + kChunkData + 4 * (8 * (r >> 4) + (r & 7)));
+            dequant_rowgroup(make_uint4(w0[0], w0[1], w0[2], w0[3]), (sc >> (8 * odd)) & 0xFF, v0);
+            dequant_rowgroup(make_uint4(w1[0], w1[1], w1[2], w1[3]), (sc >> (16 + 8 * odd)) & 0xFF, v1);
+          }
+          if (MXFP4_TC_DIAG & 2) {
+          } else if constexpr (kTS) {
+            tc_fence_after();
+            const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + kTmemARingCol + s * 32;
+            tmem_st16(ta, v0);
+            tmem_st16(ta + 16, v1);
+            tmem_wait_st();
+            tc_fence_before();
+          } else {
+            const uint32_t at = smem_u32(smem + Cfg::kOffA + s * Cfg::kATileBytes) + r * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              sts128(at + ((j ^ (r & 7)) << 4), make_uint4(v0[4 * j], v0[4 * j + 1], v0[4 * j + 2], v0[4 * j + 3]));
+              sts128(at + (((4 + j) ^ (r & 7)) << 4),
+                     make_uint4(v1[4 * j], v1[4 * j + 1], v1[4 * j + 2], v1[4 * j + 3]));
+            }
+            fence_proxy_async_smem();
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dqd[s]);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&dqd[s]);
         if (++s == S) {
           s = 0;
           ph ^= 1;
