@@ -12,6 +12,7 @@
 #include "common.cuh"
 #include "gemm_large.cuh"
 #include "gemm_small.cuh"
+#include "gemm_small_tc.cuh"
 #include "quant.cuh"
 
 namespace mxb {
@@ -28,6 +29,7 @@ struct DeviceState {
   int major = 0;
   bool tc_attr[4] = {false, false, false, false};
   bool gv_attr[4] = {false, false, false, false};
+  bool gt_attr[2] = {false, false};
 };
 
 constexpr int kMaxDevices = 64;
@@ -274,10 +276,58 @@ int launch_gemv_t(const void* A, const uint8_t* wpack, const OutSpec& o, int M, 
 // kernel stages them itself): f16 [k_blocks*64] x M plus M row shifts.
 size_t gemv_prestage_bytes(int M, int N, int K) {
   (void)N;
-  static const int knob = env_knob("MXFP4_GEMV_PRESTAGE");  // sweeps: -1 never, 1 always
-  const int min_m = knob < 0 ? 1 << 30 : (knob > 0 ? 1 : 4);
-  if (M < min_m || M > 16) return 0;
-  return static_cast<size_t>(k_blocks_of(K)) * 128 * M + 256;
+  if (M < 1 || M > 16) return 0;
+  return static_cast<size_t>(k_blocks_of(K)) * kGtXChunkBytes + 256;  // covers both kernels' layouts
+}
+
+// Which decode kernel runs when the activations can be prestaged: gemv_kernel (mma.sync) by
+// default; MXFP4_GEMV_KERNEL=2 selects gemv_tc_kernel (tcgen05).  Measured on B200, M = 1..16:
+// the tcgen05 kernel reaches 1.0-1.9 TB/s against 2.0-4.4 TB/s for gemv_kernel, so it is kept
+// as an alternative, not the default.
+bool gemv_use_tc() {
+  static const int knob = env_knob("MXFP4_GEMV_KERNEL");
+  return knob == 2;
+}
+
+template <typename OutT>
+int launch_gemv_tc_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K, int sm_count,
+                     cudaStream_t stream, DeviceState* d, const uint8_t* xpre, const int* xshift) {
+  const int slot = sizeof(OutT) == 4 ? 0 : 1;
+  if (!d->gt_attr[slot]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GtCfg::kSmemBytes);
+    if (e != cudaSuccess) return ret(e);
+    d->gt_attr[slot] = true;
+  }
+  const int nb = n_blocks_of(N), kb = k_blocks_of(K);
+  int ks = 1;
+  while (ks < 8 && nb * ks < 3 * sm_count && ceil_div(kb, ks * 2) >= kGtStageChunks) ks *= 2;
+  static const int ks_knob = env_knob("MXFP4_GEMV_KS");
+  if (ks_knob == 1 || ks_knob == 2 || ks_knob == 4 || ks_knob == 8) ks = ks_knob;
+  const int kbps = ceil_div(kb, ks);
+  GvOut<OutT> out;
+  std::memset(&out, 0, sizeof(out));
+  for (int i = 0; i < o.count; ++i) out.p[i] = static_cast<OutT*>(o.dst[i]);
+  out.count = o.count;
+  out.ldc = o.ldc;
+  out.n_off = o.n_off;
+  out.fence_sys = o.fence_sys;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nb, ks, 1);
+  cfg.blockDim = dim3(kGtThreads, 1, 1);
+  cfg.dynamicSmemBytes = GtCfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = ks;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // after our prestage kernel
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tc_kernel<OutT>, wpack, M, kb, kbps, xpre, xshift, out, N);
+  return ret(e);
 }
 
 int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
@@ -290,10 +340,24 @@ int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dty
   if (need && xws && xws_bytes >= need && aligned16(xws)) {
     xpre = xws;
     xshift = reinterpret_cast<int*>(xws + need - 256);
-    gemv_prestage_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, k_blocks_of(K), xpre,
-                                                xshift);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return ret(e);
+    if (gemv_use_tc()) {
+      gemv_prestage_tc_kernel<<<16, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, k_blocks_of(K),
+                                                      xpre, xshift);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return ret(e);
+      return c_dtype == MXFP4_DTYPE_F32
+                 ? launch_gemv_tc_t<float>(wpack, C, M, N, K, d->sm_count, stream, d, xpre, xshift)
+                 : launch_gemv_tc_t<__nv_bfloat16>(wpack, C, M, N, K, d->sm_count, stream, d, xpre, xshift);
+    }
+    if (M >= 4) {  // the mma.sync kernel stages small M itself
+      gemv_prestage_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, k_blocks_of(K),
+                                                  xpre, xshift);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return ret(e);
+    } else {
+      xpre = nullptr;
+      xshift = nullptr;
+    }
   }
   if (p.nt == 1)
     return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<1, float>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift)

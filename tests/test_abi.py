@@ -39,11 +39,12 @@ def test_abi_version_and_queries(L):
     # 3072 x 3072: 24 x 48 chunks of 4352 bytes = packed + scales exactly
     assert lib.mxfp4_prepacked_bytes(3072, 3072) == 3072 * 3072 // 2 + 3072 * 3072 // 32
     assert lib.mxfp4_prepacked_bytes(200, 96) == 2 * 2 * 4352
-    # prepacked weights need no workspace for large M; decode shapes (M <= 16) get optional room
-    # for the activations converted once per call: f16 [K/64 * 64] x M plus 256 bytes of row shifts
+    # prepacked weights need no workspace for large M (no GPU here, so no split-K plan); decode
+    # shapes (M <= 16) get optional room for the activations converted once per call: one 2 KiB
+    # f16 block (16 rows x 64 k) per 64-k chunk plus 256 bytes of row shifts
     assert lib.mxfp4_gemm_workspace_bytes(32, 3072, 3072, L.LAYOUT_PREPACKED) == 0
-    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_PREPACKED) == 48 * 128 * 8 + 256
-    assert lib.mxfp4_gemm_workspace_bytes(2, 3072, 3072, L.LAYOUT_PREPACKED) == 0
+    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_PREPACKED) == 48 * 2048 + 256
+    assert lib.mxfp4_gemm_workspace_bytes(1, 3072, 3072, L.LAYOUT_PREPACKED) == 48 * 2048 + 256
     assert lib.mxfp4_gemm_workspace_bytes(32, 3072, 3072, L.LAYOUT_REF) == lib.mxfp4_prepacked_bytes(3072, 3072)
     assert lib.mxfp4_select_path(1, 8192, 8192) == L.PATH_GEMV
     assert lib.mxfp4_select_path(16, 8192, 8192) == L.PATH_GEMV

@@ -195,3 +195,28 @@ def test_tc_split_k_matches_unsplit(mx, path, M, N, K):
             torch.cuda.synchronize()
             assert mx.device_error() == 0
             assert rel_err(C.float().cpu().numpy(), ref) <= TOL, (dtype, ws_bytes)
+
+
+def test_tcgen05_decode_kernel_opt_in():
+    """The tcgen05 decode kernel (selected with MXFP4_GEMV_KERNEL=2, read once per process) meets
+    the same bound; run in a child process so the knob does not leak into other tests."""
+    import subprocess
+    import sys
+
+    code = (
+        "import sys, numpy as np, torch; sys.path[:0] = ['tests', 'oracle', 'cdna3-bench_b200'];"
+        "import mxfp4_b200 as mx, mxfp4_ref as o; from _util import make_case, rel_err\n"
+        "for M, N, K in ((1, 1024, 2048), (5, 384, 8192), (16, 200, 96)):\n"
+        "    A, Bp, Bs = make_case(M, N, K, seed=M + N)\n"
+        "    w = mx.prepack_b200(Bp, Bs)\n"
+        "    C = mx.gemm(torch.from_numpy(A).to(torch.bfloat16).cuda(), w, out_dtype=torch.float32, path='gemv')\n"
+        "    torch.cuda.synchronize(); assert mx.device_error() == 0\n"
+        "    e = rel_err(C.cpu().numpy(), o.ref_gemm(A, Bp, Bs)); assert e <= 1e-2, (M, N, K, e)\n"
+        "print('ok')\n"
+    )
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300,
+                       env={**os.environ, "MXFP4_GEMV_KERNEL": "2"})
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
