@@ -3,6 +3,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -24,12 +25,16 @@ inline int ret(cudaError_t e) { return e == cudaSuccess ? 0 : static_cast<int>(e
 
 inline int launch_status() { return ret(cudaGetLastError()); }
 
+// Per-device facts queried once.  `ready` is published after sm_count and major are written;
+// the *_attr flags only skip repeating an idempotent cudaFuncSetAttribute, so concurrent
+// first calls at worst repeat it.
 struct DeviceState {
+  std::atomic<bool> ready{false};
   int sm_count = 0;
   int major = 0;
-  bool tc_attr[4] = {false, false, false, false};
-  bool gv_attr[4] = {false, false, false, false};
-  bool gt_attr[2] = {false, false};
+  std::atomic<bool> tc_attr[4] = {false, false, false, false};
+  std::atomic<bool> gv_attr[4] = {false, false, false, false};
+  std::atomic<bool> gt_attr[2] = {false, false};
 };
 
 constexpr int kMaxDevices = 64;
@@ -42,15 +47,16 @@ int current_device(DeviceState** st) {
   if (e != cudaSuccess) return ret(e);
   if (dev < 0 || dev >= kMaxDevices) return MXFP4_ERR_DEVICE;
   DeviceState& d = g_dev[dev];
-  if (d.sm_count == 0) {
+  if (!d.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(g_mu);
-    if (d.sm_count == 0) {
+    if (!d.ready.load(std::memory_order_relaxed)) {
       int sms = 0, major = 0;
       e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
       if (e != cudaSuccess) return ret(e);
       d.major = major;
       d.sm_count = sms;
+      d.ready.store(true, std::memory_order_release);
     }
   }
   if (d.major != 10) return MXFP4_ERR_DEVICE;
