@@ -2,6 +2,7 @@
 
     python -m mxfp4_b200.bench [--shapes M,N,K ...] [--out results/sweep.csv]
                                [--warmup 50] [--iters 100]
+    python -m mxfp4_b200.bench --quantize [K,N ...]      # GPU quantiser + prepack throughput
 
 Mirrors python/mxfp4_cdna3/bench.py:31-119 (_bench_one, run_sweep): seed-0 inputs
 (A ~ N(0,1) bf16, W ~ N(0,1) quantised along K), 8 rotating weight copies, one CUDA event
@@ -98,6 +99,39 @@ def run_sweep(shapes, out_csv, n_warmup: int = 50, n_iter: int = 100, rot: int =
     return rows
 
 
+def bench_quantize(shapes, n_iter: int = 20, rule: str = "ocp") -> list[dict]:
+    """GPU quantiser + prepack throughput (the reference does both on the host in NumPy,
+    ref.py:14-47 and :85-101).  Bytes = fp32 input read + packed nibbles and scales written,
+    and for the prepack the packed weights read + the chunk layout written."""
+    dev = torch.device("cuda:0")
+    peaks = cm.load_peaks()
+    out = []
+    for K, N in shapes:
+        W = torch.randn(K, N, device=dev) * 0.02
+        Bp, Bs = kk.quantize_mxfp4(W, axis=0, rule=rule)
+        kk.prepack_b200(Bp, Bs)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        for _ in range(n_iter):
+            kk.quantize_mxfp4(W, axis=0, rule=rule)
+        ev[1].record()
+        for _ in range(n_iter):
+            kk.prepack_b200(Bp, Bs)
+        ev[2].record()
+        torch.cuda.synchronize()
+        tq = ev[0].elapsed_time(ev[1]) / n_iter * 1e3
+        tp = ev[1].elapsed_time(ev[2]) / n_iter * 1e3
+        qbytes = K * N * 4 + K * N // 2 + K * N // 32
+        pbytes = 2 * (K * N // 2 + K * N // 32)
+        row = {"K": K, "N": N, "quantize_us": tq, "quantize_gbs": qbytes / tq / 1e3,
+               "prepack_us": tp, "prepack_gbs": pbytes / tp / 1e3, "hbm_peak_gbs": peaks.hbm_gbs}
+        log.info("quantize %dx%d: %.1f us %.0f GB/s | prepack %.1f us %.0f GB/s (HBM copy peak %.0f)",
+                 K, N, tq, row["quantize_gbs"], tp, row["prepack_gbs"], peaks.hbm_gbs)
+        out.append(row)
+    return out
+
+
 def summarize(rows) -> dict:
     """(strategy, M, N, K) -> p50 ns, from run_sweep rows."""
     acc: dict = {}
@@ -112,9 +146,14 @@ def main(argv=None) -> None:
     ap.add_argument("--out", default="results/sweep.csv")
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--iters", type=int, default=100)
+    ap.add_argument("--quantize", nargs="*", default=None, metavar="K,N",
+                    help="time the GPU quantiser and prepack on K x N fp32 weights instead of the GEMM sweep")
     ap.add_argument("--log-level", default="INFO")
     args = ap.parse_args(argv)
     logging.basicConfig(level=args.log_level, format="%(asctime)s %(levelname)s %(name)s: %(message)s")
+    if args.quantize is not None:
+        bench_quantize([tuple(int(x) for x in s.split(",")) for s in (args.quantize or ["3072,3072", "8192,57344"])])
+        return
     shapes = [tuple(int(x) for x in s.split(",")) for s in args.shapes]
     run_sweep(shapes, args.out, args.warmup, args.iters)
 

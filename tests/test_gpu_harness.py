@@ -61,3 +61,10 @@ def test_column_parallel_single_process_slices():
         parts.append(Y)
     full = sharding.assemble(parts, N).cpu().numpy()
     assert rel_err(full, ref) <= 1e-2
+
+
+def test_quantize_bench_runs():
+    from mxfp4_b200 import bench
+
+    rows = bench.bench_quantize([(256, 384)], n_iter=2)
+    assert rows[0]["quantize_gbs"] > 0 and rows[0]["prepack_gbs"] > 0
