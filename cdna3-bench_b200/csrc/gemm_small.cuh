@@ -38,19 +38,25 @@ namespace mxb {
 #endif
 constexpr int kGvThreads = 288;     // 8 compute warps + 1 producer warp
 constexpr int kGvStageChunks = 4;   // chunks per bulk copy / ring stage
-constexpr int kGvStageBytes = kGvStageChunks * kChunkBytes;
+constexpr int kGvStageWBytes = kGvStageChunks * kChunkBytes;  // weights of one stage
 constexpr int kGvMaxStages = 8;
 
 template <int NT>
 struct GvCfg {
   static constexpr int kMP = 8 * NT;  // padded activation rows
-  // [ring: stages x kGvStageBytes; reused for the partial sums once drained][full/empty
-  // barriers][xshift, abort, xmax][staged x: two 32-groups x M rows x 16 f16 pairs per chunk]
-  __host__ __device__ static int off_bar(int stages) { return stages * kGvStageBytes; }
-  __host__ __device__ static int off_shift(int stages) { return off_bar(stages) + (2 * kGvMaxStages + 2) * 8; }
-  __host__ __device__ static int off_x(int stages) { return (off_shift(stages) + 8 * kMP + 16 + 127) & ~127; }
-  __host__ __device__ static int smem_bytes(int stages, int kb_per_split, int M) {
-    return off_x(stages) + kb_per_split * 2 * M * 64;
+  // [ring: stages x stage_bytes; reused for the partial sums once drained][full/empty
+  // barriers][xshift, abort, xmax][activations staged in-kernel: two 32-groups x M rows x 16 f16
+  // pairs per chunk].  With prestaged activations each stage carries its chunks' activation
+  // blocks after the weights and there is no separate activation region.
+  __host__ __device__ static int stage_bytes(int M, bool prestaged) {
+    return kGvStageChunks * (kChunkBytes + (prestaged ? 2 * M * 64 : 0));
+  }
+  __host__ __device__ static int off_bar(int stages, int sb) { return stages * sb; }
+  __host__ __device__ static int off_shift(int stages, int sb) { return off_bar(stages, sb) + (2 * kGvMaxStages + 2) * 8; }
+  __host__ __device__ static int off_x(int stages, int sb) { return (off_shift(stages, sb) + 8 * kMP + 16 + 127) & ~127; }
+  __host__ __device__ static int smem_bytes(int stages, int kb_per_split, int M, bool prestaged) {
+    const int sb = stage_bytes(M, prestaged);
+    return off_x(stages, sb) + (prestaged ? 0 : kb_per_split * 2 * M * 64);
   }
 };
 
@@ -110,14 +116,15 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
   constexpr int MP = Cfg::kMP;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::off_bar(stages));
+  const bool pre = xpre != nullptr;
+  const int sbytes = Cfg::stage_bytes(M, pre);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::off_bar(stages, sbytes));
   uint64_t* empty = full + kGvMaxStages;
-  uint64_t* xbar = empty + kGvMaxStages;  // prestaged activations landed
-  int* xshift = reinterpret_cast<int*>(smem + Cfg::off_shift(stages));
+  int* xshift = reinterpret_cast<int*>(smem + Cfg::off_shift(stages, sbytes));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(xshift + MP);
   unsigned* xmax = reinterpret_cast<unsigned*>(xshift + MP + 4);  // per-row max |x| (float bits)
   float* red = reinterpret_cast<float*>(smem);  // aliases the drained ring
-  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Cfg::off_x(stages));
+  uint32_t* xs = reinterpret_cast<uint32_t*>(smem + Cfg::off_x(stages, sbytes));
 
   const int nb = blockIdx.x;
   const int split = blockIdx.y;
@@ -132,7 +139,6 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 8);
     }
-    mbar_init(xbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -145,33 +151,33 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
       const uint8_t* src = wpack + (static_cast<size_t>(nb) * k_blocks + kb0) * kChunkBytes;
       uint32_t pend = 0, pend_ph = 0;
       bool aborted = false;
-      // Prestaged activations (written by the launch just before this one): the weight
-      // stages that need no free slot go out first, then -- once that launch has finished --
-      // one bulk copy of this CTA's slice of the staged activations.
-      const uint32_t xbytes = static_cast<uint32_t>(nkb) * 2 * M * 64;
-      const int x_at = min(stages, nst);
-      bool x_pending = xpre != nullptr && xbytes > 0;
-      auto issue_x = [&]() {
-        griddep_wait();
-        mbar_arrive_expect_tx(xbar, xbytes);
-        bulk_load(xs, xpre + static_cast<size_t>(kb0) * 2 * M * 64, xbytes, xbar);
-        x_pending = false;
-      };
+      // With prestaged activations (written by the launch just before this one) each stage also
+      // carries its chunks' activation blocks; the first weight copy goes out before waiting
+      // for that launch to finish.
+      const uint32_t xblk = 2u * M * 64;
+      bool waited = false;
       for (int i = 0; i < nst; ++i) {
-        if (x_pending && i == x_at) issue_x();
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
           aborted = true;
           break;
         }
-        const uint32_t bytes = min(kGvStageChunks, nkb - i * kGvStageChunks) * kChunkBytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_load(ring + s * kGvStageBytes, src + static_cast<size_t>(i) * kGvStageBytes, bytes, &full[s]);
+        const uint32_t nch = min(kGvStageChunks, nkb - i * kGvStageChunks);
+        mbar_arrive_expect_tx(&full[s], nch * (kChunkBytes + (pre ? xblk : 0u)));
+        bulk_load(ring + s * sbytes, src + static_cast<size_t>(i) * kGvStageWBytes, nch * kChunkBytes, &full[s]);
+        if (pre) {
+          if (!waited) {
+            griddep_wait();
+            waited = true;
+          }
+          bulk_load(ring + s * sbytes + kGvStageWBytes,
+                    xpre + (static_cast<size_t>(kb0) + static_cast<size_t>(i) * kGvStageChunks) * xblk, nch * xblk,
+                    &full[s]);
+        }
         pend |= 1u << s;
         pend_ph = (pend_ph & ~(1u << s)) | (ph << s);
       }
-      if (x_pending) issue_x();  // also when aborted: the consumers may be waiting on it
       if (aborted)
         for (int i = 0; i < stages; ++i)
           if ((pend >> i) & 1) mbar_wait_drain(&full[i], (pend_ph >> i) & 1);
@@ -190,10 +196,9 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     // the word stores spread over the banks (the prestaged layout of gemv_prestage_kernel is the
     // same with kg in place of grp).  Only the M real rows are staged; the MMA lanes of padding
     // rows use zero registers.
-    if (xpre != nullptr) {
+    if (pre) {
       griddep_wait();
       if (threadIdx.x < MP) xshift[threadIdx.x] = threadIdx.x < M ? xpre_shift[threadIdx.x] : 0;
-      if (nkb > 0) warp_wait(xbar, 0, kErrWaitFull, abort_flag);
     } else if (!(MXFP4_GV_DIAG & 8)) {
       const int k_lo = kb0 * 64;
       const int nvec = nkb * 8;  // 16-byte vectors (8 bf16) per row in the staged range
@@ -275,7 +280,7 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     // activation block of (local group xg, row 8*jt + g) for this lane: lane_x[xg & 3] + xg*M*64 + jt*512
     uint32_t lane_x[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) lane_x[j] = xs_a + g * 64 + (t ^ ((j + 2 * kb0) & 3)) * 16;
+    for (int j = 0; j < 4; ++j) lane_x[j] = g * 64 + (t ^ ((j + 2 * kb0) & 3)) * 16;
     const uint32_t m64 = static_cast<uint32_t>(M) * 64;
     bool row_live[NT];
 #pragma unroll
@@ -283,8 +288,10 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     for (int i = 0; i < nst; ++i) {
       const int s = i % stages;
       if (!warp_wait(&full[s], (i / stages) & 1, kErrWaitFull, abort_flag)) break;
-      const uint32_t st = ring_a + s * kGvStageBytes;
-      const uint32_t xstage = static_cast<uint32_t>(i) * (2 * kGvStageChunks) * m64;
+      const uint32_t st = ring_a + s * sbytes;
+      // activation blocks of this stage's chunks (2*M*64 bytes each): in the stage after the
+      // weights when prestaged, else in the staged region
+      const uint32_t xstage = pre ? st + kGvStageWBytes : xs_a + static_cast<uint32_t>(i) * (2 * kGvStageChunks) * m64;
 #pragma unroll
       for (int c = 0; c < kGvStageChunks; ++c) {
         const int ci = i * kGvStageChunks + c;

@@ -235,7 +235,7 @@ GvPlan plan_gemv(int M, int N, int K, int sm_count) {
   if (ks_knob == 1 || ks_knob == 2 || ks_knob == 4 || ks_knob == 8) p.ks = ks_knob;
   if (st_knob >= 2 && st_knob <= kGvMaxStages) p.stages = st_knob;
   p.kbps = ceil_div(kb, p.ks);
-  p.smem = p.nt == 1 ? GvCfg<1>::smem_bytes(p.stages, p.kbps, M) : GvCfg<2>::smem_bytes(p.stages, p.kbps, M);
+  p.smem = p.nt == 1 ? GvCfg<1>::smem_bytes(p.stages, p.kbps, M, false) : GvCfg<2>::smem_bytes(p.stages, p.kbps, M, false);
   return p;
 }
 
@@ -338,8 +338,7 @@ int launch_gemv_tc_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K
 
 int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
                 cudaStream_t stream, DeviceState* d, uint8_t* xws, size_t xws_bytes) {
-  const GvPlan p = plan_gemv(M, N, K, d->sm_count);
-  if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  GvPlan p = plan_gemv(M, N, K, d->sm_count);
   const size_t need = gemv_prestage_bytes(M, N, K);
   uint8_t* xpre = nullptr;
   int* xshift = nullptr;
@@ -355,7 +354,9 @@ int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dty
                  ? launch_gemv_tc_t<float>(wpack, C, M, N, K, d->sm_count, stream, d, xpre, xshift)
                  : launch_gemv_tc_t<__nv_bfloat16>(wpack, C, M, N, K, d->sm_count, stream, d, xpre, xshift);
     }
-    if (M >= 4) {  // the mma.sync kernel stages small M itself
+    static const int min_m_knob = env_knob("MXFP4_GEMV_PRESTAGE_MIN_M");  // sweeps
+    const int min_m = min_m_knob > 0 ? min_m_knob : 4;
+    if (M >= min_m) {  // below it the mma.sync kernel stages the few rows itself
       gemv_prestage_kernel<<<M, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, k_blocks_of(K),
                                                   xpre, xshift);
       cudaError_t e = cudaGetLastError();
@@ -365,6 +366,9 @@ int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dty
       xshift = nullptr;
     }
   }
+  if (xpre)  // activations travel in the weight ring: no staged-activation region
+    p.smem = p.nt == 1 ? GvCfg<1>::smem_bytes(p.stages, p.kbps, M, true) : GvCfg<2>::smem_bytes(p.stages, p.kbps, M, true);
+  if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
   if (p.nt == 1)
     return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_t<1, float>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift)
                                       : launch_gemv_t<1, __nv_bfloat16>(A, wpack, C, M, N, K, p, stream, d, xpre, xshift);
