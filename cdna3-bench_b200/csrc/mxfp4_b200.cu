@@ -366,7 +366,18 @@ int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dty
       xshift = nullptr;
     }
   }
-  if (xpre)  // activations travel in the weight ring: no staged-activation region
+  if (xpre) {  // activations travel in the weight ring: no staged-activation region
+    // K-split for this case, measured on B200: each CTA's K range at most 64 chunks, and at least
+    // 1.5 CTAs per SM (gate+up 57344 x 8192: 2 splits; 8192- and 10240-row shapes: 4).
+    const int nb = n_blocks_of(N), kb = k_blocks_of(K);
+    int ks = 1;
+    while (ks < 8 && (ceil_div(kb, ks) > 64 || 2 * nb * ks < 3 * d->sm_count)) ks *= 2;
+    static const int ks_knob = env_knob("MXFP4_GEMV_KS");
+    if (ks_knob == 1 || ks_knob == 2 || ks_knob == 4 || ks_knob == 8) ks = ks_knob;
+    p.ks = ks;
+    p.kbps = ceil_div(kb, ks);
+  }
+  if (xpre)
     p.smem = p.nt == 1 ? GvCfg<1>::smem_bytes(p.stages, p.kbps, M, true) : GvCfg<2>::smem_bytes(p.stages, p.kbps, M, true);
   if (p.smem > 232448 - 1024) return MXFP4_ERR_UNSUPPORTED_SHAPE;
   if (p.nt == 1)
