@@ -26,17 +26,12 @@
 
 namespace mxb {
 
-#ifndef MXFP4_GV_MINB
-#define MXFP4_GV_MINB 4
-#endif
-#ifndef MXFP4_GV_MMA_VOLATILE
-#define MXFP4_GV_MMA_VOLATILE 0
-#endif
 #ifndef MXFP4_GV_DIAG
 #define MXFP4_GV_DIAG 0  // sweep-only bitmask: 1 = skip the E2M1 conversion, 2 = skip the scale decode,
                          // 4 = skip the MMAs, 8 = skip the activation staging
 #endif
 constexpr int kGvThreads = 288;     // 8 compute warps + 1 producer warp
+constexpr int kGvMinBlocks = 4;     // register cap so that four CTAs fit on an SM
 constexpr int kGvStageChunks = 4;   // chunks per bulk copy / ring stage
 constexpr int kGvStageWBytes = kGvStageChunks * kChunkBytes;  // weights of one stage
 constexpr int kGvMaxStages = 8;
@@ -65,12 +60,8 @@ __device__ __forceinline__ float exp2i(int e) { return __uint_as_float(static_ca
 
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
-#if MXFP4_GV_MMA_VOLATILE
-  asm volatile(
-#else
-  asm(
-#endif
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+  // not volatile: the compiler may interleave independent MMAs with the conversions
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -108,7 +99,7 @@ struct GvOut {
 };
 
 template <int NT, typename OutT>
-__global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
+__global__ void __launch_bounds__(kGvThreads, kGvMinBlocks)
     gemv_kernel(const __nv_bfloat16* __restrict__ A, int M, int K, const uint8_t* __restrict__ wpack,
                 int k_blocks, int kb_per_split, int stages, const GvOut<OutT> out, int N,
                 const uint8_t* __restrict__ xpre, const int* __restrict__ xpre_shift) {
@@ -364,7 +355,9 @@ __global__ void __launch_bounds__(kGvThreads, MXFP4_GV_MINB)
     const int n = nb * kChunkRows + row;
     if (n < N) {
       const OutT v = gv_out<OutT>(sum);
-      for (int d = 0; d < out.count; ++d) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
+#pragma unroll
+      for (int d = 0; d < 8; ++d)  // fixed trip count: out.p stays in the parameter space
+        if (d < out.count) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
     }
   }
   if (out.fence_sys) __threadfence_system();

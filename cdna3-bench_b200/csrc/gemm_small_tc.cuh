@@ -266,7 +266,9 @@ __global__ void __launch_bounds__(kGtThreads)
     const int n = nb * kChunkRows + row;
     if (n < N) {
       const OutT v = gv_out<OutT>(sum);
-      for (int d = 0; d < out.count; ++d) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
+#pragma unroll
+      for (int d = 0; d < 8; ++d)  // fixed trip count: out.p stays in the parameter space
+        if (d < out.count) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
     }
   }
   if (out.fence_sys) __threadfence_system();
