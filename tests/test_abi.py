@@ -68,3 +68,14 @@ def test_invalid_arguments_rejected_before_any_launch(L):
     assert lib.mxfp4_quantize(P(16), 33, 32, 0, 0, P(16), P(16), None) == 1001
     assert lib.mxfp4_prepack(P(16), P(16), 100, 64, 2, P(16), None) == 1001  # G needs N % 128
     assert "workspace" in L.error_string(1003)
+
+
+def test_python_cost_model_agrees_with_library_path_choice(L):
+    """cost_model.pick_path (Python, the reference's cost_model.py counterpart) and the
+    library's mxfp4_select_path pick the same kernel family on a grid of shapes."""
+    from mxfp4_b200 import cost_model as cm
+
+    names = {v: k for k, v in L.PATH_NAMES.items()}
+    for M in (1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 4608, 8192):
+        for N, K in ((3072, 3072), (8192, 8192), (57344, 8192), (1024, 28672), (9216, 3072)):
+            assert cm.pick_path(cm.Shape(M, N, K)) == names[L.lib().mxfp4_select_path(M, N, K)], (M, N, K)
