@@ -55,6 +55,17 @@ def test_tc_paths_match_oracle(mx, path, M, N, K):
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 9, 16])
 @pytest.mark.parametrize("N,K", [(1024, 2048), (200, 96), (384, 8192)])
 def test_gemv_path_matches_oracle(mx, M, N, K):
+    _check_gemv(mx, M, N, K)
+
+
+@pytest.mark.parametrize("M,N,K", [(3, 8, 32), (16, 136, 32), (7, 4096, 224), (5, 264, 28672 + 32),
+                                   (12, 1152, 160)])
+def test_gemv_edge_shapes(mx, M, N, K):
+    """Tiny N (one 8-column group), K of half a chunk, ragged K tails and long K."""
+    _check_gemv(mx, M, N, K)
+
+
+def _check_gemv(mx, M, N, K):
     A, Bp, Bs = make_case(M, N, K, seed=M + N + K)
     ref = o.ref_gemm(A, Bp, Bs)
     C32 = _run(mx, A, Bp, Bs, "gemv", torch.float32)
