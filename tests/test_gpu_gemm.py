@@ -179,7 +179,8 @@ def test_gemv_without_workspace_stages_in_kernel(mx, M):
 
 
 @pytest.mark.parametrize("path", ["tc", "tc_smem"])
-@pytest.mark.parametrize("M,N,K", [(128, 3072, 3072), (64, 640, 4096), (200, 256, 1024), (300, 1024, 8192)])
+@pytest.mark.parametrize("M,N,K", [(128, 3072, 3072), (64, 640, 4096), (200, 256, 1024), (300, 1024, 8192),
+                                   (40, 136, 4160)])
 def test_tc_split_k_matches_unsplit(mx, path, M, N, K):
     """Few tiles (small M x N): with workspace the large-M kernel splits K into fp32 partials
     and reduces them; without workspace it runs unsplit.  Both meet the bound, fp32 and bf16."""
