@@ -26,12 +26,18 @@ constexpr int kChunkData = kChunkRows * kChunkK / 2;                     // 4096
 constexpr int kChunkBytes = kChunkData + kChunkRows * (kChunkK / kGroup);  // + 256 B scales
 
 // Chunk byte layout.  Word t (bytes b = 0..3 hold k-pairs t + 4b of the group) of row r's
-// 32-group grp sits in 16-byte unit 32*(r/16) + 4*(r%8) + t, at word 2*grp + (r/8)%2: one unit
-// holds the four A-fragment words lane (g = r%8, t) of an m16n8k16 MMA needs for rows
-// 16*(r/16) .. +15 and both groups.  The scales follow the data in the same order, four to a
-// 4-byte unit 8*(r/16) + r%8.
+// 32-group grp sits at word 2*grp + (r/8)%2 of 16-byte unit chunk_unit(r, t): one unit holds
+// the four A-fragment words lane (g = r%8, t) of an m16n8k16 MMA needs for rows 16*(r/16) .. +15
+// and both groups.  Inside each 32-unit block (rows 16a .. 16a+15) unit (k = r%8, t) sits at
+// position 8t + ((k + 2t) mod 8), so that both access patterns are free of shared-memory bank
+// conflicts: the decode kernel's 8-lane phases (k in {2p, 2p+1}, t = 0..3) and the large-M
+// kernel's (k = 0..7, one t) each touch 8 different 16-byte bank groups.  The scales follow the
+// data, four to a 4-byte unit 8*(r/16) + r%8.
+__host__ __device__ constexpr int chunk_unit(int r, int t) {
+  return 32 * (r >> 4) + 8 * t + (((r & 7) + 2 * t) & 7);
+}
 __host__ __device__ constexpr int chunk_word_off(int r, int grp, int t) {
-  return (32 * (r >> 4) + 4 * (r & 7) + t) * 16 + (2 * grp + ((r >> 3) & 1)) * 4;
+  return chunk_unit(r, t) * 16 + (2 * grp + ((r >> 3) & 1)) * 4;
 }
 __host__ __device__ constexpr int chunk_scale_off(int r, int grp) {
   return kChunkData + 4 * (8 * (r >> 4) + (r & 7)) + 2 * grp + ((r >> 3) & 1);

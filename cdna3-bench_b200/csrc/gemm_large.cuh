@@ -342,15 +342,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ------------------------------------------------------------ dequant
     // Two groups of four warps take the pipeline steps in turn (group 0 the even ones, group 1
     // the odd ones); in its step a warp dequantises both 32-element groups of its 32 rows.  Lane
-    // r reads the four 16-byte units t = 0..3 of its row (each unit holds word t of rows r and
-    // r^8 in both groups; lanes r and r^8 read the same unit, so a warp's loads are 16 distinct
-    // units, free of bank conflicts) and keeps the words of its own row.
+    // r reads the four 16-byte units chunk_unit(r, t), t = 0..3 (each holds word t of rows r and
+    // r^8 in both groups; lanes r and r^8 share a unit and the unit placement puts each 8-lane
+    // phase on distinct bank groups) and keeps the words of its own row.
     const int q = warp & 3;
     const int grp = (warp - kTcFirstDqWarp) >> 2;
     const int r = 32 * q + lane;  // weight row inside the tile == TMEM lane
     const int odd = (r >> 3) & 1;
     const uint32_t wbase = smem_u32(smem + Cfg::kOffW);
-    const uint32_t unit0 = (32 * (r >> 4) + 4 * (r & 7)) * 16;
     int s = 0;
     uint32_t ph = 0, it = 0;
     bool aborted = false;
@@ -372,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t w0[4], w1[4];
 #pragma unroll
             for (int tt = 0; tt < 4; ++tt) {
-              const uint4 u = lds128(wst + unit0 + tt * 16);
+              const uint4 u = lds128(wst + chunk_unit(r, tt) * 16);
               w0[tt] = odd ? u.y : u.x;  // (row, group 0)
               w1[tt] = odd ? u.w : u.z;  // (row, group 1)
             }

@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kGvThreads, kGvMinBlocks)
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
     const uint32_t ring_a = smem_u32(ring);
     const uint32_t xs_a = smem_u32(xs);
-    const uint32_t lane_d = (32 * warp + lane) * 16;
+    const uint32_t lane_d = chunk_unit(16 * warp + g, t) * 16;  // this lane's fragment unit
     const uint32_t lane_s = kChunkData + (8 * warp + g) * 4;
     // activation block of (local group xg, row 8*jt + g) for this lane: lane_x[xg & 3] + xg*M*64 + jt*512
     uint32_t lane_x[4];

@@ -159,7 +159,6 @@ __global__ void __launch_bounds__(kGtThreads)
     const int q = warp & 3;
     const int r = 32 * q + lane;  // weight row == TMEM lane
     const int odd = (r >> 3) & 1;
-    const uint32_t unit0 = (32 * (r >> 4) + 4 * (r & 7)) * 16;
     const uint32_t lane_t = static_cast<uint32_t>(32 * q) << 16;
     float acc[16];
 #pragma unroll
@@ -193,7 +192,7 @@ __global__ void __launch_bounds__(kGtThreads)
       uint32_t w0[4], w1[4];
 #pragma unroll
       for (int tt = 0; tt < 4; ++tt) {
-        const uint4 u = lds128(st + unit0 + tt * 16);
+        const uint4 u = lds128(st + chunk_unit(r, tt) * 16);
         w0[tt] = odd ? u.y : u.x;  // (row, group 0)
         w1[tt] = odd ? u.w : u.z;  // (row, group 1)
       }

@@ -168,13 +168,14 @@ def chunk_data_offset(r, grp, t, b):
     word t (0..3) and byte b (0..3) of that row-group, where byte b of word t holds the
     nibble pair for k-pair t + 4*b of the group (low nibble = even k).
 
-    16-byte units u = 32*w + 4*g + t, with w = r // 16 and g = r % 8, each hold word t of
-    (row 16w+g, group 0), (row 16w+g+8, group 0), (row 16w+g, group 1), (row 16w+g+8, group 1):
-    exactly the A-fragment words lane (g, t) of an m16n8k16 MMA needs for rows 16w..16w+15,
-    so a decode kernel fetches them with one 16-byte load per lane.
+    The 16-byte unit of (k = r % 8, t) in the 32-unit block of rows 16a .. 16a+15 (a = r // 16)
+    holds word t of (row 16a+k, group 0), (row 16a+k+8, group 0), (row 16a+k, group 1),
+    (row 16a+k+8, group 1): the A-fragment words lane (k, t) of an m16n8k16 MMA needs.  It sits
+    at unit position 32a + 8t + ((k + 2t) mod 8) (a placement free of shared-memory bank
+    conflicts for both kernels' access patterns).
     """
     r = np.asarray(r)
-    unit = 32 * (r >> 4) + 4 * (r & 7) + t
+    unit = 32 * (r >> 4) + 8 * t + (((r & 7) + 2 * t) & 7)
     word = 2 * grp + ((r >> 3) & 1)
     return unit * 16 + word * 4 + b
 
