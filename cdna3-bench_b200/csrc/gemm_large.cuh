@@ -234,7 +234,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int mb, nb, kb_lo, kb_hi, ks;
       tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
-      if (!warp_wait(acc_full, aph, kErrWaitAccFull, abort_flag)) break;
+      bool ok = warp_wait(acc_full, aph, kErrWaitAccFull, abort_flag);
+      // The two warps of a bf16 slab pair meet at a named barrier below: they leave the loop
+      // together (if either gave up waiting), or neither does.
+      if (sizeof(OutT) == 2 && out.count > 1) ok = named_bar_and(2 + (ew >> 1), 64, ok);
+      if (!ok) break;
       tc_fence_after();
       const int m0 = mb * kTcTileAct + 128 * hh;  // activation rows m0 .. m0+127 of this warp
       const int n0 = nb * kTcTileW + 32 * q;      // output columns n0 .. n0+31 (one per lane)
