@@ -12,6 +12,7 @@
 #include "../../include/mxfp4_b200.h"
 #include "common.cuh"
 #include "gemm_large.cuh"
+#include "gemm_mx.cuh"
 #include "gemm_small.cuh"
 #include "gemm_small_tc.cuh"
 #include "quant.cuh"
@@ -35,6 +36,7 @@ struct DeviceState {
   std::atomic<bool> tc_attr[4] = {false, false, false, false};
   std::atomic<bool> gv_attr[4] = {false, false, false, false};
   std::atomic<bool> gt_attr[2] = {false, false};
+  std::atomic<bool> mx_attr[2] = {false, false};
 };
 
 constexpr int kMaxDevices = 64;
@@ -401,6 +403,79 @@ int do_prepack(const uint8_t* packed, const uint8_t* scales, int N, int K, int l
   return launch_status();
 }
 
+// ------------------------------------------------------------------ block-scaled path
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Re-laid weights of the block-scaled path: nibbles [Np][Kp/2], then the scale blocks.
+size_t mx_weight_data_bytes(int N, int K) {
+  return static_cast<size_t>(round_up(N, kTcTileW)) * (round_up(K, kMxBK) / 2);
+}
+size_t mx_weight_bytes(int N, int K) {
+  return mx_weight_data_bytes(N, K) + static_cast<size_t>(round_up(N, kTcTileW)) * (round_up(K, kMxBK) / kGroup);
+}
+// Quantised activations: E4M3 [M][Kp], then (256-byte aligned) the scale blocks of Ma rows.
+size_t mx_act_data_bytes(int M, int K) { return align256(static_cast<size_t>(M) * round_up(K, kMxBK)); }
+size_t mx_act_bytes(int M, int K) {
+  return mx_act_data_bytes(M, K) + static_cast<size_t>(round_up(M, kTcTileAct)) * (round_up(K, kMxBK) / kGroup);
+}
+
+int quantize_act_mx8(const void* A, int M, int K, uint8_t* dst, cudaStream_t stream) {
+  const int Kp = round_up(K, kMxBK), Ma = round_up(M, kTcTileAct);
+  const long long work = static_cast<long long>(Ma) * (Kp / kGroup);
+  const int threads = 256;
+  quant_act_mx8_kernel<<<static_cast<unsigned>((work + threads - 1) / threads), threads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(A), M, K, Kp, Ma, dst, dst + mx_act_data_bytes(M, K));
+  return launch_status();
+}
+
+// 2-D map over 4-bit values [outer][inner] (rows of inner/2 bytes) that the TMA expands to
+// 16-byte units holding 8 bytes of data, the shared-memory form of an E2M1 kind::mxf8f6f4
+// operand.  inner is a multiple of 128 and the base 32-byte aligned.
+int encode_2d_e2m1_expanded(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                            uint32_t box_outer) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return MXFP4_ERR_DRIVER;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner / 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
+}
+
+template <typename OutT>
+int launch_mx(const uint8_t* a8, const uint8_t* wmx, void* C, int M, int N, int K, cudaStream_t stream,
+              DeviceState* d) {
+  using Cfg = MxCfg<OutT>;
+  const int slot = sizeof(OutT) == 4 ? 0 : 1;
+  if (!d->mx_attr[slot]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_mx_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return ret(e);
+    d->mx_attr[slot] = true;
+  }
+  const int Kp = round_up(K, kMxBK), Np = round_up(N, kTcTileW);
+  CUtensorMap tm_act, tm_w, tm_out;
+  int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a8, Kp, M, kMxBK, kTcTileAct,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d_e2m1_expanded(&tm_w, wmx, Kp, Np, kMxBK, kTcTileW);
+  if (rc) return rc;
+  rc = encode_2d_strided(&tm_out, sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         static_cast<int>(sizeof(OutT)), C, N, M, static_cast<uint64_t>(N) * sizeof(OutT), 32, 32);
+  if (rc) return rc;
+  const int m_blocks = ceil_div(M, kTcTileAct), n_blocks = Np / kTcTileW;
+  const int tiles = m_blocks * n_blocks;
+  const int grid = std::min(tiles, d->sm_count);
+  gemm_mx_kernel<OutT><<<grid, kMxThreads, Cfg::kSmemBytes, stream>>>(
+      tm_act, tm_w, tm_out, wmx + mx_weight_data_bytes(N, K), a8 + mx_act_data_bytes(M, K), M, Kp / kMxBK, m_blocks,
+      n_blocks);
+  return launch_status();
+}
+
 }  // namespace
 }  // namespace mxb
 
@@ -562,6 +637,67 @@ size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
   DeviceState* d = nullptr;
   const size_t sk = M > 16 && current_device(&d) == 0 ? splitk_bytes(M, N, K, d->sm_count) : 0;
   return pre + std::max(x, sk);
+}
+
+// ------------------------------------------------------------------ block-scaled path
+size_t mxfp4_mx_weight_bytes(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  return mx_weight_bytes(N, K);
+}
+
+int mxfp4_prepack_mx(const uint8_t* packed, const uint8_t* scales, int N, int K, int src_layout, uint8_t* dst,
+                     void* stream) {
+  if (!packed || !scales || !dst || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (src_layout != MXFP4_LAYOUT_REF && src_layout != MXFP4_LAYOUT_NK) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (reinterpret_cast<uintptr_t>(dst) & 31u) return MXFP4_ERR_MISALIGNED;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int Np = round_up(N, kTcTileW), Kp = round_up(K, kMxBK);
+  const int threads = 256;
+  const long long dwork = static_cast<long long>(Np) * (Kp / 32), swork = static_cast<long long>(Np) * (Kp / kMxBK);
+  const unsigned db = static_cast<unsigned>((dwork + threads - 1) / threads);
+  const unsigned sb = static_cast<unsigned>((swork + threads - 1) / threads);
+  uint8_t* sfa = dst + mx_weight_data_bytes(N, K);
+  if (src_layout == MXFP4_LAYOUT_REF) {
+    prepack_mx_data_kernel<true><<<db, threads, 0, s>>>(packed, N, K, Np, Kp, dst);
+    prepack_mx_scale_kernel<true><<<sb, threads, 0, s>>>(scales, N, K, Np, Kp, sfa);
+  } else {
+    prepack_mx_data_kernel<false><<<db, threads, 0, s>>>(packed, N, K, Np, Kp, dst);
+    prepack_mx_scale_kernel<false><<<sb, threads, 0, s>>>(scales, N, K, Np, Kp, sfa);
+  }
+  return launch_status();
+}
+
+size_t mxfp4_mx_workspace_bytes(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  return mx_act_bytes(M, K);
+}
+
+int mxfp4_quantize_act_mx8(const void* A, int M, int K, uint8_t* dst, void* stream) {
+  if (!A || !dst || M <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!aligned16(A) || !aligned16(dst)) return MXFP4_ERR_MISALIGNED;
+  return quantize_act_mx8(A, M, K, dst, static_cast<cudaStream_t>(stream));
+}
+
+int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int M, int N, int K, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (!A || !w_mx || !C || M <= 0 || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (c_dtype != MXFP4_DTYPE_F32 && c_dtype != MXFP4_DTYPE_BF16) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (K % kGroup || N % 8) return MXFP4_ERR_UNSUPPORTED_SHAPE;
+  if (!workspace || workspace_bytes < mx_act_bytes(M, K)) return MXFP4_ERR_WORKSPACE;
+  if (!aligned16(A) || !aligned16(C) || (reinterpret_cast<uintptr_t>(w_mx) & 31u) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 31u))
+    return MXFP4_ERR_MISALIGNED;
+  DeviceState* d = nullptr;
+  int rc = current_device(&d);
+  if (rc) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  uint8_t* a8 = static_cast<uint8_t*>(workspace);
+  rc = quantize_act_mx8(A, M, K, a8, s);
+  if (rc) return rc;
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_mx<float>(a8, w_mx, C, M, N, K, s, d)
+                                    : launch_mx<__nv_bfloat16>(a8, w_mx, C, M, N, K, s, d);
 }
 
 }  // extern "C"

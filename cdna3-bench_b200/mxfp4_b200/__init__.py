@@ -43,6 +43,10 @@ _OPS = (
     "shape_supported_g",
     "device_info",
     "device_error",
+    "MXWeight",
+    "prepack_mx",
+    "quantize_act_mx8",
+    "gemm_mx",
 )
 
 __all__ = list(_OPS)

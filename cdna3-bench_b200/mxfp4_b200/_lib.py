@@ -42,6 +42,11 @@ EXPORTED = (
     "mxfp4_ipc_export",
     "mxfp4_ipc_open",
     "mxfp4_ipc_close",
+    "mxfp4_mx_weight_bytes",
+    "mxfp4_prepack_mx",
+    "mxfp4_mx_workspace_bytes",
+    "mxfp4_quantize_act_mx8",
+    "mxfp4_gemm_mx",
 )
 
 
@@ -91,6 +96,11 @@ def _declare(lib):
         "mxfp4_ipc_export": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
         "mxfp4_ipc_open": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
         "mxfp4_ipc_close": (_I, [_P, _SZ]),
+        "mxfp4_mx_weight_bytes": (_SZ, [_I, _I]),
+        "mxfp4_prepack_mx": (_I, [_P, _P, _I, _I, _I, _P, _P]),
+        "mxfp4_mx_workspace_bytes": (_SZ, [_I, _I]),
+        "mxfp4_quantize_act_mx8": (_I, [_P, _I, _I, _P, _P]),
+        "mxfp4_gemm_mx": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -431,3 +431,71 @@ def device_error(clear: bool = True) -> int:
     code = ctypes.c_uint(0)
     _lib.check(_lib.lib().mxfp4_device_error(int(clear), ctypes.byref(code)), "mxfp4_device_error")
     return code.value
+
+
+# ----------------------------------------------------------------------------- block-scaled path
+# Opt-in: activations quantised to MXFP8 (E4M3) and both scales applied by the tensor core's
+# block-scaled MMA.  Not the exact path: compare against dequant(Q8(A)) @ dequant(W).
+
+
+@dataclass
+class MXWeight:
+    """Weights in the block-scaled path's layout (nibbles [Np][Kp/2] + scale blocks)."""
+
+    data: torch.Tensor  # uint8, mxfp4_mx_weight_bytes(N, K) bytes
+    N: int
+    K: int
+
+
+def prepack_mx(B_packed, B_scales, layout: str = "ref") -> MXWeight:
+    """Re-lay MXFP4 weights (layout "ref": [K/2, N] + [K/32, N]; "nk": [N, K/2] + [N, K/32])
+    for :func:`gemm_mx`."""
+    p = _to_device(B_packed, torch.uint8)
+    s = _to_device(B_scales, torch.uint8)
+    _check(layout in ("ref", "nk"), "prepack_mx: layout must be 'ref' or 'nk'")
+    if layout == "ref":
+        K, N = p.shape[0] * 2, p.shape[1]
+    else:
+        N, K = p.shape[0], p.shape[1] * 2
+    L = _lib.lib()
+    out = torch.empty(L.mxfp4_mx_weight_bytes(N, K), dtype=torch.uint8, device=p.device)
+    _lib.check(L.mxfp4_prepack_mx(_ptr(p), _ptr(s), N, K, _LAYOUTS[layout], _ptr(out), _stream()), "mxfp4_prepack_mx")
+    return MXWeight(out, N, K)
+
+
+def _mx_sizes(M: int, K: int):
+    Kp = -(-K // 128) * 128
+    Ma = -(-M // 256) * 256
+    data = -(-(M * Kp) // 256) * 256
+    return Kp, Ma, data
+
+
+def quantize_act_mx8(A: torch.Tensor):
+    """MXFP8 (E4M3) quantisation of bf16 A[M, K] as the block-scaled GEMM does it.
+    Returns (codes uint8 [M, Kp], scale blocks uint8 [Kp/128, Ma/128, 512])."""
+    _check_A(A)
+    M, K = A.shape
+    L = _lib.lib()
+    Kp, Ma, data = _mx_sizes(M, K)
+    ws = torch.empty(L.mxfp4_mx_workspace_bytes(M, K), dtype=torch.uint8, device=A.device)
+    _lib.check(L.mxfp4_quantize_act_mx8(_ptr(A), M, K, _ptr(ws), _stream()), "mxfp4_quantize_act_mx8")
+    codes = ws[: M * Kp].view(M, Kp)
+    blocks = ws[data:].view(Kp // 128, Ma // 128, 512)
+    return codes, blocks
+
+
+def gemm_mx(A: torch.Tensor, w: MXWeight, out_dtype=torch.bfloat16, C=None):
+    """C[M, N] = Q8(A) @ dequant(w)^T on the block-scaled tensor-core path."""
+    _check_A(A, w.K)
+    M = A.shape[0]
+    if C is None:
+        C = torch.empty((M, w.N), dtype=out_dtype, device=A.device)
+    _check(C.is_cuda and C.dtype in _ODT and tuple(C.shape) == (M, w.N) and C.is_contiguous(), "C shape/contig")
+    L = _lib.lib()
+    nws = L.mxfp4_mx_workspace_bytes(M, w.K)
+    ws = torch.empty(nws, dtype=torch.uint8, device=A.device)
+    _lib.check(
+        L.mxfp4_gemm_mx(_ptr(A), _ptr(w.data), _ptr(C), _ODT[C.dtype], M, w.N, w.K, _ptr(ws), nws, _stream()),
+        "mxfp4_gemm_mx",
+    )
+    return C

@@ -229,3 +229,126 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
 
 def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---------------------------------------------------------------------------------------
+# Block-scaled path (an extension with no reference counterpart).  The activations are
+# quantised to OCP MXFP8 (E4M3 elements, one E8M0 scale per 32 k of a row) and the result is
+# dequant(Q8(A)) @ dequant(W).  The E4M3 codec is pinned against torch.float8_e4m3fn in
+# tests/test_oracle.py; the scale rule follows the OCP Microscaling Formats v1.0 spec:
+# X = 2**(floor(log2(amax)) - emax_elem), emax_elem = 8 for E4M3 (largest normal 448 = 1.75 * 2**8).
+
+E4M3_EMAX = 8
+E4M3_MAX = 448.0
+MX_BK = 128  # k per 128-row scale block (4 groups of 32)
+MX_SF_BLOCK = 512
+
+
+def e4m3_values() -> np.ndarray:
+    """float32 value of every E4M3 (fn variant) code 0..255; 0x7F and 0xFF are NaN."""
+    c = np.arange(256)
+    s = np.where(c >> 7, -1.0, 1.0)
+    e = (c >> 3) & 15
+    m = (c & 7).astype(np.float64)
+    mag = np.where(e == 0, m * 2.0**-9, (1.0 + m / 8.0) * np.exp2(e - 7.0))
+    v = (s * mag).astype(np.float32)
+    v[(c & 0x7F) == 0x7F] = np.nan
+    return v
+
+
+def encode_e4m3(x) -> np.ndarray:
+    """fp32 -> E4M3 codes: round to nearest, ties to the even code, magnitudes above 448
+    saturate to 448 (the cvt.rn.satfinite rule); the sign of x is kept (also for zero)."""
+    x = np.asarray(x, dtype=np.float32)
+    mags = e4m3_values()[:127].astype(np.float64)  # codes 0..126, ascending
+    a = np.minimum(np.abs(x).astype(np.float64), E4M3_MAX)
+    hi = np.clip(np.searchsorted(mags, a, side="left"), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    dlo, dhi = a - mags[lo], mags[hi] - a
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo).astype(np.uint8)
+    code = np.where(a == mags[hi], hi, code).astype(np.uint8)
+    return code | (np.signbit(x).astype(np.uint8) << 7)
+
+
+def quantize_act_mx8(A) -> tuple[np.ndarray, np.ndarray]:
+    """OCP MXFP8 quantisation of activations A [M, K] along K (K % 32 == 0).
+
+    Scale exponent e = floor(log2(amax)) - 8, clipped to [-127, 127]; an all-zero group gets
+    e = -127 (byte 0).  Elements: encode_e4m3(x * 2**-e) (exact scaling, then RNE + saturate).
+    Returns codes uint8 [M, K] and scale bytes uint8 [M, K/32].
+    """
+    A = np.asarray(A, dtype=np.float32)
+    M, K = A.shape
+    if K % GROUP:
+        raise ValueError("K must be a multiple of 32")
+    g = A.reshape(M, K // GROUP, GROUP)
+    amax = np.abs(g).max(axis=-1)
+    _, E = np.frexp(amax)  # amax = f * 2**E, f in [0.5, 1)
+    e = np.where(amax > 0, np.clip(E.astype(np.int64) - 1 - E4M3_EMAX, -127, 127), -127)
+    scaled = (g.astype(np.float64) * np.exp2(-e.astype(np.float64))[..., None]).astype(np.float32)
+    codes = encode_e4m3(scaled).reshape(M, K)
+    return codes, (e + 127).astype(np.uint8)
+
+
+def dequantize_act_mx8(codes, scales) -> np.ndarray:
+    codes = np.asarray(codes, dtype=np.uint8)
+    M, K = codes.shape
+    v = e4m3_values()[codes].reshape(M, K // GROUP, GROUP).astype(np.float64)
+    s = np.exp2(np.asarray(scales, dtype=np.float64) - 127.0)
+    return (v * s[..., None]).reshape(M, K).astype(np.float32)
+
+
+def ref_gemm_mx(A, B_packed, B_scales) -> np.ndarray:
+    """The block-scaled path's reference: dequant(Q8(A)) @ dequant(W) in fp32 (W in the
+    reference layout [K/2, N] + [K/32, N])."""
+    codes, sc = quantize_act_mx8(A)
+    return dequantize_act_mx8(codes, sc) @ dequantize_mxfp4(B_packed, B_scales, axis=0)
+
+
+def mx_sf_in_block(r, j):
+    """Byte of (row r of a 128-row block, 32-k group j of a 128-k step) in a 512-byte scale
+    block: 16*(r%32) + 4*(r//32) + j (the tcgen05.cp 32x128b.warpx4 source order)."""
+    r = np.asarray(r)
+    return 16 * (r & 31) + 4 * ((r >> 5) & 3) + j
+
+
+def mx_scale_blocks(scales, rows_pad: int, k_pad: int, fill: int, k_major_blocks: bool) -> np.ndarray:
+    """Scale bytes [rows, K/32] -> 512-byte blocks.  k_major_blocks=False: [rows_pad/128][k_pad/128]
+    (weights); True: [k_pad/128][rows_pad/128] (activations).  Padding bytes = fill."""
+    scales = np.asarray(scales, dtype=np.uint8)
+    rows, kg = scales.shape
+    full = np.full((rows_pad, k_pad // GROUP), fill, dtype=np.uint8)
+    full[:rows, :kg] = scales
+    rb, kb = rows_pad // 128, k_pad // MX_BK
+    r, j = np.meshgrid(np.arange(128), np.arange(4), indexing="ij")
+    off = mx_sf_in_block(r, j).reshape(-1)
+    src = full.reshape(rb, 128, kb, 4).transpose(0, 2, 1, 3).reshape(rb, kb, 512)  # [rb, kb, r*4+j]
+    out = np.empty((rb, kb, 512), dtype=np.uint8)
+    out[:, :, off] = src
+    return out.transpose(1, 0, 2).copy() if k_major_blocks else out
+
+
+def mx_weight_layout(B_packed, B_scales) -> np.ndarray:
+    """Host restatement of mxfp4_prepack_mx for reference-layout weights: nibbles [Np][Kp/2]
+    (row n = weight column n, K contiguous, zero padded) then the scale blocks
+    [Np/128][Kp/128] (padding scale 127); flat uint8."""
+    B_packed = np.asarray(B_packed, dtype=np.uint8)
+    K2, N = B_packed.shape
+    K = 2 * K2
+    Np, Kp = -(-N // 128) * 128, -(-K // MX_BK) * MX_BK
+    data = np.zeros((Np, Kp // 2), dtype=np.uint8)
+    data[:N, :K2] = B_packed.T
+    sf = mx_scale_blocks(np.asarray(B_scales, dtype=np.uint8).T, Np, Kp, 127, False)
+    return np.concatenate([data.reshape(-1), sf.reshape(-1)])
+
+
+def mx_act_layout(codes, scales) -> tuple[np.ndarray, np.ndarray]:
+    """Host restatement of mxfp4_quantize_act_mx8's output: codes [M][Kp] (zero padded) and
+    scale blocks [Kp/128][Ma/128][512] (padding byte 0), Ma = M rounded up to 256."""
+    codes = np.asarray(codes, dtype=np.uint8)
+    M, K = codes.shape
+    Kp, Ma = -(-K // MX_BK) * MX_BK, -(-M // 256) * 256
+    c = np.zeros((M, Kp), dtype=np.uint8)
+    c[:, :K] = codes
+    return c, mx_scale_blocks(scales, Ma, Kp, 0, True)
