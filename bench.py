@@ -73,6 +73,9 @@ def parse():
     ap.add_argument("--workload", default="flux_ds", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--mx", action="store_true",
+                    help="opt-in block-scaled path (activations quantised to MXFP8, kind::mxf8f6f4 MMA; "
+                         "different numerics): flux_ds / flux_ss only, no e2e or CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="all-gather outputs (column-parallel)")
     ap.add_argument("--unfused", action="store_true",
@@ -270,6 +273,10 @@ def main():
         return float(t.item())
 
     metric, unit = METRICS[args.workload]
+    if args.mx:
+        if args.workload not in ("flux_ds", "flux_ss") or world > 1:
+            raise SystemExit("--mx: flux_ds or flux_ss on one GPU")
+        metric, args.no_e2e, args.no_cpu_baseline = metric + "_mx", True, True
     M, gemms = shapes_for(args.workload, world)
     decode = is_decode(args.workload)
     scale = unit_scale(args.workload)
@@ -282,7 +289,7 @@ def main():
         Bp, Bs = mx.quantize_mxfp4(W, axis=0, rule="ocp")
         del W
         items.append({"name": name, "N": N, "K": K, "A": A, "Bp": Bp, "Bs": Bs,
-                      "w": mx.prepack_b200(Bp, Bs),
+                      "w": mx.prepack_b200(Bp, Bs), "wmx": kk.prepack_mx(Bp, Bs) if args.mx else None,
                       "C": torch.empty((M, N), dtype=torch.bfloat16, device=dev)})
     flops_step = sum(2.0 * M * it["N"] * it["K"] for it in items)
     bytes_step = sum(cost_model.Shape(M, it["N"], it["K"]).in_bytes for it in items)
@@ -324,6 +331,8 @@ def main():
                 ev[i_step][j][0].record()
             if fused is not None:
                 kk.gemm_allgather(it["A"], w, fused[j].ptrs, offs[j], fused[j].N)
+            elif args.mx:
+                kk.gemm_mx(it["A"], it["wmx"], C=it["C"])
             else:
                 mx.gemm(it["A"], w, C=it["C"])
             if record:
@@ -436,13 +445,20 @@ def main():
         roof = {"bound": "hbm", "achieved": ach, "peak": peaks.hbm_gbs, "unit": "GB/s",
                 "frac": ach / peaks.hbm_gbs, "kernel": "gemv_kernel",
                 "peak_source": f"{peaks.source} hbm_gbs (copy)"}
+    elif args.mx:  # 8-bit MMA: no fp8 GEMM is measured on this pool; its nominal rate is twice bf16
+        ach = flops_step / (sum(launch_ms) * 1e-3) / 1e12
+        pk = 2.0 * (peaks.bf16_tflops_sustained if sustained else peaks.bf16_tflops)
+        roof = {"bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
+                "kernel": "quant_act_mx8_kernel + gemm_mx_kernel",
+                "peak_source": f"2 x {peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16 "
+                               "(the 8-bit MMA rate is twice the 16-bit one)"}
     else:
         ach = flops_step / (sum(launch_ms) * 1e-3) / 1e12
         pk = peaks.bf16_tflops_sustained if sustained else peaks.bf16_tflops
         roof = {"bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
                 "kernel": "gemm_tc_kernel",
                 "peak_source": f"{peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16"}
-    roof["traffic"] = load_traffic(args.workload)
+    roof["traffic"] = None if args.mx else load_traffic(args.workload)
     if fused is not None:  # the fused GEMM + all-gather: compute or NVLink, whichever is slower
         link_gbs = 770.0  # measured peer copy per direction on this pool's B200s
         sent = sum(M * it["N"] * 2 * (world - 1) for it in items)
@@ -477,6 +493,8 @@ def main():
                 "workload": args.workload, "M": M,
                 "gemms": [[it["name"], it["N"], it["K"]] for it in items],
                 "weights": "MXFP4 (E2M1 + E8M0/32), prepacked, resident in HBM",
+                "activations": ("quantised to MXFP8 (E4M3 + E8M0/32) inside each step, block-scaled MMA"
+                                if args.mx else "bf16"),
                 "output": "bf16", "accumulate": "fp32",
                 "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if small
                        else "inputs larger than L2: one step touches "
@@ -490,7 +508,7 @@ def main():
                                 else f"weak x{world}, per-rank N-slice, no collective"),
             },
             "roofline": roof, "per_gemm": per_gemm, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": args.steps * sum(1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
+            "gpu_launches": args.steps * sum(2 if args.mx else 1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
                                              for it in items), "clocks": sampler.summary(),
         }), flush=True)
     if world > 1:
