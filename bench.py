@@ -73,9 +73,9 @@ def parse():
     ap.add_argument("--workload", default="flux_ds", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--mx", action="store_true",
-                    help="opt-in block-scaled path (activations quantised to MXFP8, kind::mxf8f6f4 MMA; "
-                         "different numerics): flux_ds / flux_ss only, no e2e or CPU baseline")
+    ap.add_argument("--mx", choices=["q8", "split2"], default=None,
+                    help="block-scaled path (activations coded as E4M3 pieces, kind::mxf8f6f4 MMA; q8: one "
+                         "OCP MXFP8 piece, split2: two pieces): one GPU, no e2e or CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--allgather", action="store_true", help="all-gather outputs (column-parallel)")
     ap.add_argument("--unfused", action="store_true",
@@ -274,9 +274,9 @@ def main():
 
     metric, unit = METRICS[args.workload]
     if args.mx:
-        if args.workload not in ("flux_ds", "flux_ss") or world > 1:
-            raise SystemExit("--mx: flux_ds or flux_ss on one GPU")
-        metric, args.no_e2e, args.no_cpu_baseline = metric + "_mx", True, True
+        if args.workload in ("flux_chain", "tp_sweep") or world > 1:
+            raise SystemExit("--mx: flux_ds, flux_ss, c0 or decode_* on one GPU")
+        metric, args.no_e2e, args.no_cpu_baseline = f"{metric}_mx_{args.mx}", True, True
     M, gemms = shapes_for(args.workload, world)
     decode = is_decode(args.workload)
     scale = unit_scale(args.workload)
@@ -305,6 +305,15 @@ def main():
         for it in items:
             it["w_rot"] = [it["w"]] + [mx.MXFP4Weight(it["w"].data.clone(), it["w"].N, it["w"].K)
                                        for _ in range(rot - 1)]
+            if args.mx:
+                it["w_rot"] = [it["wmx"]] + [kk.MXWeight(it["wmx"].data.clone(), it["N"], it["K"])
+                                             for _ in range(rot - 1)]
+
+    def run_gemm(it, w):
+        """One GEMM of the step on the selected path (w: the weights in that path's layout)."""
+        if args.mx:
+            return kk.gemm_mx(it["A"], w, mode=args.mx, C=it["C"])
+        return mx.gemm(it["A"], w, C=it["C"])
 
     gather = fused = None
     if world > 1 and (args.allgather or args.workload == "tp_sweep"):
@@ -326,15 +335,13 @@ def main():
 
     def step(i_step: int, record: bool):
         for j, it in enumerate(items):
-            w = it["w_rot"][i_step % rot] if small else it["w"]
+            w = it["w_rot"][i_step % rot] if small else (it["wmx"] if args.mx else it["w"])
             if record:
                 ev[i_step][j][0].record()
             if fused is not None:
                 kk.gemm_allgather(it["A"], w, fused[j].ptrs, offs[j], fused[j].N)
-            elif args.mx:
-                kk.gemm_mx(it["A"], it["wmx"], C=it["C"])
             else:
-                mx.gemm(it["A"], w, C=it["C"])
+                run_gemm(it, w)
             if record:
                 ev[i_step][j][1].record()
             if fused is not None:
@@ -398,7 +405,7 @@ def main():
             with torch.cuda.graph(g):
                 for j, it in enumerate(items):
                     evs[j][0].record()
-                    mx.gemm(it["A"], it["w_rot"][r], C=it["C"])
+                    run_gemm(it, it["w_rot"][r])
                     evs[j][1].record()
             graphs.append(g)
             gev.append(evs)
@@ -444,6 +451,11 @@ def main():
         ach = bytes_step / (sum(launch_ms) * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": peaks.hbm_gbs, "unit": "GB/s",
                 "frac": ach / peaks.hbm_gbs, "kernel": "gemv_kernel",
+                "peak_source": f"{peaks.source} hbm_gbs (copy)"}
+    elif args.mx and decode:
+        ach = bytes_step / (sum(launch_ms) * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": ach, "peak": peaks.hbm_gbs, "unit": "GB/s",
+                "frac": ach / peaks.hbm_gbs, "kernel": "quant_act_mx8_kernel + gemv_mx_kernel (+ finalize)",
                 "peak_source": f"{peaks.source} hbm_gbs (copy)"}
     elif args.mx:  # 8-bit MMA: no fp8 GEMM is measured on this pool; its nominal rate is twice bf16
         ach = flops_step / (sum(launch_ms) * 1e-3) / 1e12
@@ -493,7 +505,7 @@ def main():
                 "workload": args.workload, "M": M,
                 "gemms": [[it["name"], it["N"], it["K"]] for it in items],
                 "weights": "MXFP4 (E2M1 + E8M0/32), prepacked, resident in HBM",
-                "activations": ("quantised to MXFP8 (E4M3 + E8M0/32) inside each step, block-scaled MMA"
+                "activations": (f"coded inside each step as E4M3 pieces + E8M0/32 ({args.mx}), block-scaled MMA"
                                 if args.mx else "bf16"),
                 "output": "bf16", "accumulate": "fp32",
                 "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if small
@@ -508,7 +520,8 @@ def main():
                                 else f"weak x{world}, per-rank N-slice, no collective"),
             },
             "roofline": roof, "per_gemm": per_gemm, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": args.steps * sum(2 if args.mx else 1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
+            "gpu_launches": args.steps * sum((3 if decode else 2) if args.mx
+                                             else 1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
                                              for it in items), "clocks": sampler.summary(),
         }), flush=True)
     if world > 1:

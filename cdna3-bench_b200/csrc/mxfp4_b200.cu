@@ -36,7 +36,8 @@ struct DeviceState {
   std::atomic<bool> tc_attr[4] = {false, false, false, false};
   std::atomic<bool> gv_attr[4] = {false, false, false, false};
   std::atomic<bool> gt_attr[2] = {false, false};
-  std::atomic<bool> mx_attr[2] = {false, false};
+  std::atomic<bool> mx_attr[4] = {false, false, false, false};
+  std::atomic<bool> gm_attr{false};
 };
 
 constexpr int kMaxDevices = 64;
@@ -414,18 +415,44 @@ size_t mx_weight_data_bytes(int N, int K) {
 size_t mx_weight_bytes(int N, int K) {
   return mx_weight_data_bytes(N, K) + static_cast<size_t>(round_up(N, kTcTileW)) * (round_up(K, kMxBK) / kGroup);
 }
-// Quantised activations: E4M3 [M][Kp], then (256-byte aligned) the scale blocks of Ma rows.
-size_t mx_act_data_bytes(int M, int K) { return align256(static_cast<size_t>(M) * round_up(K, kMxBK)); }
-size_t mx_act_bytes(int M, int K) {
-  return mx_act_data_bytes(M, K) + static_cast<size_t>(round_up(M, kTcTileAct)) * (round_up(K, kMxBK) / kGroup);
+// Coded activations (layout in gemm_mx.cuh): E4M3 code rows [rows][Kp], then (256-byte
+// aligned) the scale blocks of rows_sf rows, then for the decode kernel (M <= 16) its fp32
+// accumulation buffer [M][N].
+struct MxActPlan {
+  int G, rows, rows_sf, Kp;
+  size_t codes_bytes, sf_bytes, acc_bytes;
+  size_t sf_off() const { return codes_bytes; }
+  size_t acc_off() const { return codes_bytes + align256(sf_bytes); }
+  size_t total() const { return acc_off() + acc_bytes; }
+};
+MxActPlan mx_act_plan(int M, int N, int K, int mode) {
+  MxActPlan p;
+  p.Kp = round_up(K, kMxBK);
+  if (M <= kMxDecodeM) {
+    p.G = kMxDecodeM;
+    p.rows = kGmRows;
+  } else if (mode == kMxQ8) {
+    p.G = 0;
+    p.rows = round_up(M, kMxTileB);
+  } else {
+    p.G = kMxTileB / 2;
+    p.rows = 2 * round_up(M, kMxTileB / 2);
+  }
+  p.rows_sf = round_up(p.rows, kChunkRows);
+  p.codes_bytes = align256(static_cast<size_t>(p.rows) * p.Kp);
+  p.sf_bytes = static_cast<size_t>(p.rows_sf) * (p.Kp / kGroup);
+  p.acc_bytes = M <= kMxDecodeM ? static_cast<size_t>(M) * N * 4 : 0;
+  return p;
 }
 
-int quantize_act_mx8(const void* A, int M, int K, uint8_t* dst, cudaStream_t stream) {
-  const int Kp = round_up(K, kMxBK), Ma = round_up(M, kTcTileAct);
-  const long long work = static_cast<long long>(Ma) * (Kp / kGroup);
+int code_act_mx8(const void* A, int M, int N, int K, int mode, uint8_t* dst, bool zero_acc, cudaStream_t stream) {
+  const MxActPlan p = mx_act_plan(M, N, K, mode);
+  const long long work = static_cast<long long>(p.rows_sf) * (p.Kp / kGroup);
   const int threads = 256;
+  float* acc = zero_acc && p.acc_bytes ? reinterpret_cast<float*>(dst + p.acc_off()) : nullptr;
   quant_act_mx8_kernel<<<static_cast<unsigned>((work + threads - 1) / threads), threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(A), M, K, Kp, Ma, dst, dst + mx_act_data_bytes(M, K));
+      static_cast<const __nv_bfloat16*>(A), M, K, p.Kp, p.G, mode == kMxSplit2, p.rows, p.rows_sf, dst,
+      dst + p.sf_off(), acc, acc ? static_cast<long long>(M) * N : 0);
   return launch_status();
 }
 
@@ -446,33 +473,66 @@ int encode_2d_e2m1_expanded(CUtensorMap* map, const void* base, uint64_t inner, 
   return r == CUDA_SUCCESS ? 0 : MXFP4_ERR_DRIVER;
 }
 
-template <typename OutT>
-int launch_mx(const uint8_t* a8, const uint8_t* wmx, void* C, int M, int N, int K, cudaStream_t stream,
+template <typename OutT, bool kSplit>
+int launch_mx(const uint8_t* codes, const uint8_t* wmx, void* C, int M, int N, int K, cudaStream_t stream,
               DeviceState* d) {
   using Cfg = MxCfg<OutT>;
-  const int slot = sizeof(OutT) == 4 ? 0 : 1;
+  const int slot = (sizeof(OutT) == 4 ? 0 : 1) + (kSplit ? 2 : 0);
   if (!d->mx_attr[slot]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_mx_kernel<OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(gemm_mx_kernel<OutT, kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Cfg::kSmemBytes);
     if (e != cudaSuccess) return ret(e);
     d->mx_attr[slot] = true;
   }
-  const int Kp = round_up(K, kMxBK), Np = round_up(N, kTcTileW);
+  const MxActPlan p = mx_act_plan(M, N, K, kSplit ? kMxSplit2 : kMxQ8);
+  const int Np = round_up(N, kTcTileW);
   CUtensorMap tm_act, tm_w, tm_out;
-  int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a8, Kp, M, kMxBK, kTcTileAct,
+  int rc = encode_2d(&tm_act, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, codes, p.Kp, p.rows, kMxBK, kMxTileB,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = encode_2d_e2m1_expanded(&tm_w, wmx, Kp, Np, kMxBK, kTcTileW);
+  rc = encode_2d_e2m1_expanded(&tm_w, wmx, p.Kp, Np, kMxBK, kTcTileW);
   if (rc) return rc;
   rc = encode_2d_strided(&tm_out, sizeof(OutT) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                          static_cast<int>(sizeof(OutT)), C, N, M, static_cast<uint64_t>(N) * sizeof(OutT), 32, 32);
   if (rc) return rc;
-  const int m_blocks = ceil_div(M, kTcTileAct), n_blocks = Np / kTcTileW;
-  const int tiles = m_blocks * n_blocks;
-  const int grid = std::min(tiles, d->sm_count);
-  gemm_mx_kernel<OutT><<<grid, kMxThreads, Cfg::kSmemBytes, stream>>>(
-      tm_act, tm_w, tm_out, wmx + mx_weight_data_bytes(N, K), a8 + mx_act_data_bytes(M, K), M, Kp / kMxBK, m_blocks,
+  const int m_blocks = p.rows / kMxTileB, n_blocks = Np / kTcTileW;
+  const int grid = std::min(m_blocks * n_blocks, d->sm_count);
+  gemm_mx_kernel<OutT, kSplit><<<grid, kMxThreads, Cfg::kSmemBytes, stream>>>(
+      tm_act, tm_w, tm_out, wmx + mx_weight_data_bytes(N, K), codes + p.sf_off(), M, p.Kp / kMxBK, m_blocks,
       n_blocks);
+  return launch_status();
+}
+
+// Decode (M <= 16): stream-K kernel into the zeroed fp32 buffer (C itself for fp32 output),
+// then a conversion for bf16 output.
+int launch_gemv_mx(const uint8_t* ws, const uint8_t* wmx, void* C, int c_dtype, int M, int N, int K,
+                   cudaStream_t stream, DeviceState* d) {
+  if (!d->gm_attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_mx_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GmCfg::kSmemBytes);
+    if (e != cudaSuccess) return ret(e);
+    d->gm_attr = true;
+  }
+  const MxActPlan p = mx_act_plan(M, N, K, kMxSplit2);
+  const int Np = round_up(N, kTcTileW);
+  CUtensorMap tm_w, tm_b;
+  int rc = encode_2d_e2m1_expanded(&tm_w, wmx, p.Kp, Np, kMxBK, kTcTileW);
+  if (rc) return rc;
+  rc = encode_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, ws, p.Kp, kGmRows, kMxBK, kGmRows,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  float* acc = c_dtype == MXFP4_DTYPE_F32 ? static_cast<float*>(C)
+                                          : reinterpret_cast<float*>(const_cast<uint8_t*>(ws) + p.acc_off());
+  const int n_blocks = Np / kTcTileW, k_steps = p.Kp / kMxBK;
+  const long long steps = static_cast<long long>(n_blocks) * k_steps;
+  const int grid = static_cast<int>(std::min<long long>(d->sm_count, (steps + 3) / 4));  // >= 4 steps per CTA
+  gemv_mx_kernel<<<grid, kGmThreads, GmCfg::kSmemBytes, stream>>>(tm_w, tm_b, wmx + mx_weight_data_bytes(N, K),
+                                                                 ws + p.sf_off(), acc, M, N, n_blocks, k_steps);
+  rc = launch_status();
+  if (rc || c_dtype == MXFP4_DTYPE_F32) return rc;
+  const long long n = static_cast<long long>(M) * N;
+  const int blocks = static_cast<int>(std::min<long long>((n / 2 + 255) / 256, 4LL * d->sm_count));
+  mx_finalize_kernel<<<blocks, 256, 0, stream>>>(acc, n, static_cast<__nv_bfloat16*>(C));
   return launch_status();
 }
 
@@ -668,24 +728,25 @@ int mxfp4_prepack_mx(const uint8_t* packed, const uint8_t* scales, int N, int K,
   return launch_status();
 }
 
-size_t mxfp4_mx_workspace_bytes(int M, int K) {
-  if (M <= 0 || K <= 0) return 0;
-  return mx_act_bytes(M, K);
+size_t mxfp4_mx_workspace_bytes(int M, int N, int K, int mode) {
+  if (M <= 0 || N <= 0 || K <= 0 || (mode != kMxQ8 && mode != kMxSplit2)) return 0;
+  return mx_act_plan(M, N, K, mode).total();
 }
 
-int mxfp4_quantize_act_mx8(const void* A, int M, int K, uint8_t* dst, void* stream) {
-  if (!A || !dst || M <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
+int mxfp4_quantize_act_mx8(const void* A, int M, int K, int mode, uint8_t* dst, void* stream) {
+  if (!A || !dst || M <= 0 || K <= 0 || (mode != kMxQ8 && mode != kMxSplit2)) return MXFP4_ERR_INVALID_ARGUMENT;
   if (K % kGroup) return MXFP4_ERR_UNSUPPORTED_SHAPE;
   if (!aligned16(A) || !aligned16(dst)) return MXFP4_ERR_MISALIGNED;
-  return quantize_act_mx8(A, M, K, dst, static_cast<cudaStream_t>(stream));
+  return code_act_mx8(A, M, 8, K, mode, dst, false, static_cast<cudaStream_t>(stream));
 }
 
-int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int M, int N, int K, void* workspace,
-                  size_t workspace_bytes, void* stream) {
+int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int M, int N, int K, int mode,
+                  void* workspace, size_t workspace_bytes, void* stream) {
   if (!A || !w_mx || !C || M <= 0 || N <= 0 || K <= 0) return MXFP4_ERR_INVALID_ARGUMENT;
   if (c_dtype != MXFP4_DTYPE_F32 && c_dtype != MXFP4_DTYPE_BF16) return MXFP4_ERR_INVALID_ARGUMENT;
+  if (mode != kMxQ8 && mode != kMxSplit2) return MXFP4_ERR_INVALID_ARGUMENT;
   if (K % kGroup || N % 8) return MXFP4_ERR_UNSUPPORTED_SHAPE;
-  if (!workspace || workspace_bytes < mx_act_bytes(M, K)) return MXFP4_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < mx_act_plan(M, N, K, mode).total()) return MXFP4_ERR_WORKSPACE;
   if (!aligned16(A) || !aligned16(C) || (reinterpret_cast<uintptr_t>(w_mx) & 31u) ||
       (reinterpret_cast<uintptr_t>(workspace) & 31u))
     return MXFP4_ERR_MISALIGNED;
@@ -693,11 +754,24 @@ int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int 
   int rc = current_device(&d);
   if (rc) return rc;
   auto s = static_cast<cudaStream_t>(stream);
-  uint8_t* a8 = static_cast<uint8_t*>(workspace);
-  rc = quantize_act_mx8(A, M, K, a8, s);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (M <= kMxDecodeM) {
+    // the coder also zeroes the fp32 accumulation target (C itself for fp32 output)
+    if (c_dtype == MXFP4_DTYPE_F32) {
+      rc = ret(cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 4, s));
+      if (rc) return rc;
+    }
+    rc = code_act_mx8(A, M, N, K, mode, ws, c_dtype != MXFP4_DTYPE_F32, s);
+    if (rc) return rc;
+    return launch_gemv_mx(ws, w_mx, C, c_dtype, M, N, K, s, d);
+  }
+  rc = code_act_mx8(A, M, N, K, mode, ws, false, s);
   if (rc) return rc;
-  return c_dtype == MXFP4_DTYPE_F32 ? launch_mx<float>(a8, w_mx, C, M, N, K, s, d)
-                                    : launch_mx<__nv_bfloat16>(a8, w_mx, C, M, N, K, s, d);
+  if (mode == kMxSplit2)
+    return c_dtype == MXFP4_DTYPE_F32 ? launch_mx<float, true>(ws, w_mx, C, M, N, K, s, d)
+                                      : launch_mx<__nv_bfloat16, true>(ws, w_mx, C, M, N, K, s, d);
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_mx<float, false>(ws, w_mx, C, M, N, K, s, d)
+                                    : launch_mx<__nv_bfloat16, false>(ws, w_mx, C, M, N, K, s, d);
 }
 
 }  // extern "C"

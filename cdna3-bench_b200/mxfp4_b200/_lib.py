@@ -18,6 +18,8 @@ LAYOUT_REF, LAYOUT_NK, LAYOUT_G, LAYOUT_PREPACKED = 0, 1, 2, 3
 DTYPE_F32, DTYPE_BF16 = 0, 1
 PATH_AUTO, PATH_TC, PATH_TC_SMEM, PATH_GEMV = 0, 1, 2, 3
 RULE_REF, RULE_OCP = 0, 1
+MX_Q8, MX_SPLIT2 = 0, 1
+MX_MODES = {"q8": MX_Q8, "split2": MX_SPLIT2}
 
 PATH_NAMES = {"auto": PATH_AUTO, "tc": PATH_TC, "tc_smem": PATH_TC_SMEM, "gemv": PATH_GEMV}
 
@@ -98,9 +100,9 @@ def _declare(lib):
         "mxfp4_ipc_close": (_I, [_P, _SZ]),
         "mxfp4_mx_weight_bytes": (_SZ, [_I, _I]),
         "mxfp4_prepack_mx": (_I, [_P, _P, _I, _I, _I, _P, _P]),
-        "mxfp4_mx_workspace_bytes": (_SZ, [_I, _I]),
-        "mxfp4_quantize_act_mx8": (_I, [_P, _I, _I, _P, _P]),
-        "mxfp4_gemm_mx": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+        "mxfp4_mx_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+        "mxfp4_quantize_act_mx8": (_I, [_P, _I, _I, _I, _P, _P]),
+        "mxfp4_gemm_mx": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

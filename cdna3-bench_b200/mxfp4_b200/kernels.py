@@ -433,14 +433,15 @@ def device_error(clear: bool = True) -> int:
     return code.value
 
 
-# ----------------------------------------------------------------------------- block-scaled path
-# Opt-in: activations quantised to MXFP8 (E4M3) and both scales applied by the tensor core's
-# block-scaled MMA.  Not the exact path: compare against dequant(Q8(A)) @ dequant(W).
+# ----------------------------------------------------------------------------- block-scaled paths
+# Activations coded as E4M3 pieces with E8M0 scales, both operands' scales applied by the
+# tensor core's block-scaled MMA.  mode "q8": one OCP MXFP8 piece; "split2": hi + residual,
+# every element within 2**-8 of its group max.  Reference: oracle.ref_gemm_mx.
 
 
 @dataclass
 class MXWeight:
-    """Weights in the block-scaled path's layout (nibbles [Np][Kp/2] + scale blocks)."""
+    """Weights in the block-scaled layout (nibbles [Np][Kp/2] + scale blocks)."""
 
     data: torch.Tensor  # uint8, mxfp4_mx_weight_bytes(N, K) bytes
     N: int
@@ -463,39 +464,45 @@ def prepack_mx(B_packed, B_scales, layout: str = "ref") -> MXWeight:
     return MXWeight(out, N, K)
 
 
-def _mx_sizes(M: int, K: int):
-    Kp = -(-K // 128) * 128
-    Ma = -(-M // 256) * 256
-    data = -(-(M * Kp) // 256) * 256
-    return Kp, Ma, data
+def mx_code_rows(M: int, mode: str) -> int:
+    """Code rows of the coded-activation operand (see include/mxfp4_b200.h)."""
+    if M <= 16:
+        return 32
+    return -(-M // 256) * 256 if mode == "q8" else 2 * (-(-M // 128) * 128)
 
 
-def quantize_act_mx8(A: torch.Tensor):
-    """MXFP8 (E4M3) quantisation of bf16 A[M, K] as the block-scaled GEMM does it.
-    Returns (codes uint8 [M, Kp], scale blocks uint8 [Kp/128, Ma/128, 512])."""
+def quantize_act_mx8(A: torch.Tensor, mode: str = "q8"):
+    """The block-scaled GEMM's activation coding of bf16 A[M, K].
+    Returns (codes uint8 [rows, Kp], scale blocks uint8 [Kp/128, rows_sf/128, 512])."""
     _check_A(A)
+    _check(mode in _lib.MX_MODES, "mode must be 'q8' or 'split2'")
     M, K = A.shape
     L = _lib.lib()
-    Kp, Ma, data = _mx_sizes(M, K)
-    ws = torch.empty(L.mxfp4_mx_workspace_bytes(M, K), dtype=torch.uint8, device=A.device)
-    _lib.check(L.mxfp4_quantize_act_mx8(_ptr(A), M, K, _ptr(ws), _stream()), "mxfp4_quantize_act_mx8")
-    codes = ws[: M * Kp].view(M, Kp)
-    blocks = ws[data:].view(Kp // 128, Ma // 128, 512)
+    Kp, rows = -(-K // 128) * 128, mx_code_rows(M, mode)
+    rows_sf = -(-rows // 128) * 128
+    codes_bytes = -(-(rows * Kp) // 256) * 256
+    ws = torch.empty(L.mxfp4_mx_workspace_bytes(M, 8, K, _lib.MX_MODES[mode]), dtype=torch.uint8, device=A.device)
+    _lib.check(L.mxfp4_quantize_act_mx8(_ptr(A), M, K, _lib.MX_MODES[mode], _ptr(ws), _stream()),
+               "mxfp4_quantize_act_mx8")
+    codes = ws[: rows * Kp].view(rows, Kp)
+    blocks = ws[codes_bytes: codes_bytes + rows_sf * Kp // 32].view(Kp // 128, rows_sf // 128, 512)
     return codes, blocks
 
 
-def gemm_mx(A: torch.Tensor, w: MXWeight, out_dtype=torch.bfloat16, C=None):
-    """C[M, N] = Q8(A) @ dequant(w)^T on the block-scaled tensor-core path."""
+def gemm_mx(A: torch.Tensor, w: MXWeight, out_dtype=torch.bfloat16, mode: str = "q8", C=None):
+    """C[M, N] = A' @ dequant(w)^T on the block-scaled tensor-core path (A' = A coded per `mode`)."""
     _check_A(A, w.K)
+    _check(mode in _lib.MX_MODES, "mode must be 'q8' or 'split2'")
     M = A.shape[0]
     if C is None:
         C = torch.empty((M, w.N), dtype=out_dtype, device=A.device)
     _check(C.is_cuda and C.dtype in _ODT and tuple(C.shape) == (M, w.N) and C.is_contiguous(), "C shape/contig")
     L = _lib.lib()
-    nws = L.mxfp4_mx_workspace_bytes(M, w.K)
+    md = _lib.MX_MODES[mode]
+    nws = L.mxfp4_mx_workspace_bytes(M, w.N, w.K, md)
     ws = torch.empty(nws, dtype=torch.uint8, device=A.device)
     _lib.check(
-        L.mxfp4_gemm_mx(_ptr(A), _ptr(w.data), _ptr(C), _ODT[C.dtype], M, w.N, w.K, _ptr(ws), nws, _stream()),
+        L.mxfp4_gemm_mx(_ptr(A), _ptr(w.data), _ptr(C), _ODT[C.dtype], M, w.N, w.K, md, _ptr(ws), nws, _stream()),
         "mxfp4_gemm_mx",
     )
     return C

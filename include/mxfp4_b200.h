@@ -176,30 +176,38 @@ int mxfp4_ipc_close(void* dev_ptr, size_t offset);
 int mxfp4_gemm_noalloc(const void* A, const uint8_t* B, const uint8_t* B_scales, void* C, int c_dtype,
                        int M, int N, int K, int layout, int path, void* stream);
 
-/* ---- Opt-in block-scaled path (no reference counterpart) ---------------------------------
- * C[M,N] = Q8(A) * dequant(W) on the tensor cores' block-scaled MMA: the bf16 activations are
- * quantised to OCP MXFP8 (E4M3 elements, one E8M0 scale per 32 k of a row, exponent
- * floor(log2(amax)) - 8, round to nearest even, saturate at 448) and both operands' scales
- * are applied by the MMA.  The activation rounding changes the result, so this is not the
- * exact path of mxfp4_gemm; its reference is dequant(Q8(A)) @ dequant(W) in fp32.
- * Needs K % 32 == 0 and N % 8 == 0; re-laid weights and the workspace 32-byte aligned. */
+/* ---- Block-scaled paths (no reference counterpart) ---------------------------------------
+ * C[M,N] = A' * dequant(W) on the tensor cores' block-scaled MMA (kind::mxf8f6f4): the weights
+ * stay E2M1 + E8M0 and the bf16 activations are coded as E4M3 pieces with one E8M0 scale per
+ * 32 k of a row; the MMA applies both scales.  `mode`:
+ *   MXFP4_MX_Q8      one piece, the OCP MX rule (exponent floor(log2(amax)) - 8, round to
+ *                    nearest even, saturate at 448): activations keep 4 significant bits;
+ *   MXFP4_MX_SPLIT2  two pieces, hi (exponent floor(log2(amax)) - 7) plus the exact residual
+ *                    coded the same way: every element within 2**-8 of its group's max.
+ * Reference: (sum of the dequantised pieces) @ dequant(W) in fp32.  M <= 16 runs a stream-K
+ * decode kernel, larger M a persistent tile kernel.  Needs K % 32 == 0 and N % 8 == 0; the
+ * re-laid weights and the workspace 32-byte aligned. */
+#define MXFP4_MX_Q8 0
+#define MXFP4_MX_SPLIT2 1
 
-/* Bytes of the block-scaled path's weight layout: E2M1 nibbles [Np][Kp/2] (K contiguous)
- * followed by 512-byte scale blocks [Np/128][Kp/128]; Np = N rounded up to 128, Kp = K
- * rounded up to 128. */
+/* Bytes of the block-scaled weight layout: E2M1 nibbles [Np][Kp/2] (K contiguous) followed by
+ * 512-byte scale blocks [Np/128][Kp/128]; Np = N rounded up to 128, Kp = K rounded up to 128. */
 size_t mxfp4_mx_weight_bytes(int N, int K);
 /* Re-lay REF or NK weights into that layout (dst: mxfp4_mx_weight_bytes(N, K) bytes). */
 int mxfp4_prepack_mx(const uint8_t* packed, const uint8_t* scales, int N, int K, int src_layout, uint8_t* dst,
                      void* stream);
-/* Workspace of mxfp4_gemm_mx: the quantised activations, E4M3 [M][Kp], then (at the next
- * 256-byte boundary) their scale blocks [Kp/128][Ma/128], Ma = M rounded up to 256. */
-size_t mxfp4_mx_workspace_bytes(int M, int K);
-/* Quantise bf16 A[M,K] into dst in that workspace layout (exposed for verification). */
-int mxfp4_quantize_act_mx8(const void* A, int M, int K, uint8_t* dst, void* stream);
-/* The GEMM: quantises A into `workspace`, then one persistent block-scaled tcgen05 kernel.
- * c_dtype MXFP4_DTYPE_F32 or MXFP4_DTYPE_BF16, C [M, N] row-major. */
-int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int M, int N, int K, void* workspace,
-                  size_t workspace_bytes, void* stream);
+/* Workspace of mxfp4_gemm_mx: the coded activations (E4M3 code rows [rows][Kp], then at the
+ * next 256-byte boundary their 512-byte scale blocks [Kp/128][rows rounded up to 128, /128]),
+ * then for M <= 16 an fp32 [M][N] accumulation buffer.  Code row b holds piece p of activation
+ * row m: M <= 16: b = 16p + m (32 rows); M > 16, Q8: b = m (M rounded up to 256 rows); M > 16,
+ * SPLIT2: b = 256*(m/128) + 128p + m%128 (2 * (M rounded up to 128) rows). */
+size_t mxfp4_mx_workspace_bytes(int M, int N, int K, int mode);
+/* Code bf16 A[M,K] into dst in that layout (codes and scale blocks; exposed for verification). */
+int mxfp4_quantize_act_mx8(const void* A, int M, int K, int mode, uint8_t* dst, void* stream);
+/* The GEMM: codes A into `workspace`, then the block-scaled kernel (c_dtype MXFP4_DTYPE_F32 or
+ * MXFP4_DTYPE_BF16, C [M, N] row-major). */
+int mxfp4_gemm_mx(const void* A, const uint8_t* w_mx, void* C, int c_dtype, int M, int N, int K, int mode,
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

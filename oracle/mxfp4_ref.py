@@ -271,24 +271,46 @@ def encode_e4m3(x) -> np.ndarray:
     return code | (np.signbit(x).astype(np.uint8) << 7)
 
 
-def quantize_act_mx8(A) -> tuple[np.ndarray, np.ndarray]:
-    """OCP MXFP8 quantisation of activations A [M, K] along K (K % 32 == 0).
+def _group_exponent(amax: np.ndarray, below_top: int) -> np.ndarray:
+    """floor(log2(amax)) - below_top clipped to [-127, 127]; -127 for an all-zero group."""
+    _, E = np.frexp(amax)  # amax = f * 2**E, f in [0.5, 1)
+    return np.where(amax > 0, np.clip(E.astype(np.int64) - 1 - below_top, -127, 127), -127)
 
-    Scale exponent e = floor(log2(amax)) - 8, clipped to [-127, 127]; an all-zero group gets
-    e = -127 (byte 0).  Elements: encode_e4m3(x * 2**-e) (exact scaling, then RNE + saturate).
-    Returns codes uint8 [M, K] and scale bytes uint8 [M, K/32].
+
+def _quantize_groups(g: np.ndarray, below_top: int):
+    """[..., 32] fp32 groups -> (E4M3 codes, exponents): codes = encode_e4m3(x * 2**-e)."""
+    e = _group_exponent(np.abs(g).max(axis=-1), below_top)
+    scaled = (g.astype(np.float64) * np.exp2(-e.astype(np.float64))[..., None]).astype(np.float32)
+    return encode_e4m3(scaled), e
+
+
+MX_Q8, MX_SPLIT2 = 0, 1
+
+
+def quantize_act_mx8(A, mode: int = MX_Q8):
+    """MXFP8 quantisation of activations A [M, K] along K (K % 32 == 0).
+
+    mode MX_Q8 (OCP MX): scale exponent e = floor(log2(amax)) - 8, clipped to [-127, 127], an
+    all-zero group gets e = -127 (byte 0); codes = encode_e4m3(x * 2**-e) (exact scaling, then
+    RNE + saturation at 448).  Returns [(codes uint8 [M, K], scales uint8 [M, K/32])].
+
+    mode MX_SPLIT2: two pieces, A ~ hi + lo.  hi uses e = floor(log2(amax)) - 7 (the group max
+    lands in [128, 256), no saturation); lo quantises the exact residual A - dequant(hi) by the
+    same rule.  Returns [(hi codes, hi scales), (lo codes, lo scales)].
     """
     A = np.asarray(A, dtype=np.float32)
     M, K = A.shape
     if K % GROUP:
         raise ValueError("K must be a multiple of 32")
     g = A.reshape(M, K // GROUP, GROUP)
-    amax = np.abs(g).max(axis=-1)
-    _, E = np.frexp(amax)  # amax = f * 2**E, f in [0.5, 1)
-    e = np.where(amax > 0, np.clip(E.astype(np.int64) - 1 - E4M3_EMAX, -127, 127), -127)
-    scaled = (g.astype(np.float64) * np.exp2(-e.astype(np.float64))[..., None]).astype(np.float32)
-    codes = encode_e4m3(scaled).reshape(M, K)
-    return codes, (e + 127).astype(np.uint8)
+    if mode == MX_Q8:
+        c, e = _quantize_groups(g, E4M3_EMAX)
+        return [(c.reshape(M, K), (e + 127).astype(np.uint8))]
+    ch, eh = _quantize_groups(g, E4M3_EMAX - 1)
+    vh = e4m3_values()[ch].astype(np.float64) * np.exp2(eh.astype(np.float64))[..., None]
+    r = (g.astype(np.float64) - vh).astype(np.float32)  # exact: few significant bits on both sides
+    cl, el = _quantize_groups(r, E4M3_EMAX - 1)
+    return [(ch.reshape(M, K), (eh + 127).astype(np.uint8)), (cl.reshape(M, K), (el + 127).astype(np.uint8))]
 
 
 def dequantize_act_mx8(codes, scales) -> np.ndarray:
@@ -299,11 +321,16 @@ def dequantize_act_mx8(codes, scales) -> np.ndarray:
     return (v * s[..., None]).reshape(M, K).astype(np.float32)
 
 
-def ref_gemm_mx(A, B_packed, B_scales) -> np.ndarray:
-    """The block-scaled path's reference: dequant(Q8(A)) @ dequant(W) in fp32 (W in the
-    reference layout [K/2, N] + [K/32, N])."""
-    codes, sc = quantize_act_mx8(A)
-    return dequantize_act_mx8(codes, sc) @ dequantize_mxfp4(B_packed, B_scales, axis=0)
+def dequantize_act_pieces(pieces) -> np.ndarray:
+    """Sum of the dequantised pieces (fp64 sum, rounded to fp32)."""
+    tot = sum(dequantize_act_mx8(c, s).astype(np.float64) for c, s in pieces)
+    return np.asarray(tot, dtype=np.float32)
+
+
+def ref_gemm_mx(A, B_packed, B_scales, mode: int = MX_Q8) -> np.ndarray:
+    """The block-scaled path's reference: (sum of the dequantised activation pieces) @
+    dequant(W) in fp32 (W in the reference layout [K/2, N] + [K/32, N])."""
+    return dequantize_act_pieces(quantize_act_mx8(A, mode)) @ dequantize_mxfp4(B_packed, B_scales, axis=0)
 
 
 def mx_sf_in_block(r, j):
@@ -343,12 +370,39 @@ def mx_weight_layout(B_packed, B_scales) -> np.ndarray:
     return np.concatenate([data.reshape(-1), sf.reshape(-1)])
 
 
-def mx_act_layout(codes, scales) -> tuple[np.ndarray, np.ndarray]:
-    """Host restatement of mxfp4_quantize_act_mx8's output: codes [M][Kp] (zero padded) and
-    scale blocks [Kp/128][Ma/128][512] (padding byte 0), Ma = M rounded up to 256."""
-    codes = np.asarray(codes, dtype=np.uint8)
-    M, K = codes.shape
-    Kp, Ma = -(-K // MX_BK) * MX_BK, -(-M // 256) * 256
-    c = np.zeros((M, Kp), dtype=np.uint8)
-    c[:, :K] = codes
-    return c, mx_scale_blocks(scales, Ma, Kp, 0, True)
+MX_DECODE_M = 16  # M <= 16: the decode kernel's operand of 16 hi + 16 lo rows
+
+
+def mx_act_rows(M: int, mode: int) -> tuple[int, int]:
+    """(group rows G, code rows) of the quantised-activation operand for (M, mode).
+
+    Code row b holds piece p of activation row m, b = (m // G) * 2G + p * G + m % G (pieces
+    stacked per G-row group), or b = m with one piece (G = 0):
+      M <= 16 (decode kernel), either mode: G = 16, 32 rows (the lo rows are zero for MX_Q8);
+      M > 16, MX_Q8:     G = 0, rows = M rounded up to 256;
+      M > 16, MX_SPLIT2: G = 128, rows = 2 * (M rounded up to 128).
+    """
+    if M <= MX_DECODE_M:
+        return MX_DECODE_M, 2 * MX_DECODE_M
+    if mode == MX_Q8:
+        return 0, -(-M // 256) * 256
+    return 128, 2 * (-(-M // 128) * 128)
+
+
+def mx_act_layout(A, mode: int = MX_Q8) -> tuple[np.ndarray, np.ndarray]:
+    """Host restatement of mxfp4_quantize_act_mx8(A, mode): codes [rows][Kp] (zero padded) and
+    scale blocks [Kp/128][ceil(rows/128)][512] (padding byte 0)."""
+    A = np.asarray(A, dtype=np.float32)
+    M, K = A.shape
+    Kp = -(-K // MX_BK) * MX_BK
+    G, rows = mx_act_rows(M, mode)
+    pieces = quantize_act_mx8(A, mode)
+    codes = np.zeros((rows, Kp), dtype=np.uint8)
+    sc = np.zeros((rows, K // GROUP), dtype=np.uint8)
+    m = np.arange(M)
+    for p, (c, s) in enumerate(pieces):
+        b = m if G == 0 else (m // G) * 2 * G + p * G + m % G
+        codes[b, :K] = c
+        sc[b] = s
+    rows_sf = -(-rows // 128) * 128
+    return codes, mx_scale_blocks(sc, rows_sf, Kp, 0, True)

@@ -1,6 +1,7 @@
-"""GPU parity of the opt-in block-scaled path (MXFP8 activations x MXFP4 weights on the
-tensor cores' block-scaled MMA) against its oracle: byte-exact activation quantisation and
-weight re-layout, and the GEMM within max|err|/max|ref| <= 1e-2 of dequant(Q8(A)) @ dequant(W).
+"""GPU parity of the block-scaled paths (E4M3-coded activations x MXFP4 weights on the tensor
+cores' block-scaled MMA) against their oracle: byte-exact activation coding (both modes) and
+weight re-layout, the GEMM within max|err|/max|ref| <= 1e-2 of (sum of the dequantised
+activation pieces) @ dequant(W), and the split2 mode within the same bar of the exact product.
 
 These tests run only with MXFP4_MX_GPU_TESTS=1: the path is built and its host logic is tested
 on CPU, but it has not yet had its first run on a B200, which is done deliberately, alone, on
@@ -38,15 +39,18 @@ def _no_device_error(mx):
     assert mx.device_error(clear=True) == 0
 
 
-@pytest.mark.parametrize("M,K", [(1, 128), (300, 160), (512, 3072)])
-def test_act_quant_matches_oracle(mx, M, K):
+MODES = {"q8": o.MX_Q8, "split2": o.MX_SPLIT2}
+
+
+@pytest.mark.parametrize("mode", ["q8", "split2"])
+@pytest.mark.parametrize("M,K", [(1, 128), (16, 160), (300, 160), (512, 3072)])
+def test_act_coding_matches_oracle(mx, M, K, mode):
     rng = np.random.default_rng(M + K)
     A = (rng.standard_normal((M, K)) * np.exp2(rng.integers(-12, 12, size=(M, 1)))).astype(np.float32)
     A[0, :32] = 0.0  # an all-zero group
     Ab = torch.from_numpy(A).to(torch.bfloat16)
-    c, s = o.quantize_act_mx8(Ab.float().numpy())
-    want_codes, want_blocks = o.mx_act_layout(c, s)
-    codes, blocks = mx.quantize_act_mx8(Ab.cuda())
+    want_codes, want_blocks = o.mx_act_layout(Ab.float().numpy(), MODES[mode])
+    codes, blocks = mx.quantize_act_mx8(Ab.cuda(), mode)
     np.testing.assert_array_equal(codes.cpu().numpy(), want_codes)
     np.testing.assert_array_equal(blocks.cpu().numpy(), want_blocks)
 
@@ -60,14 +64,29 @@ def test_weight_prepack_matches_oracle(mx, N, K):
     assert torch.equal(w_nk.data, w.data)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 128, 128), (300, 200, 224), (1024, 1024, 1024), (16, 384, 512)])
+@pytest.mark.parametrize("mode", ["q8", "split2"])
+@pytest.mark.parametrize("M,N,K", [(256, 128, 128), (300, 200, 224), (1024, 1024, 1024), (1, 384, 512),
+                                   (16, 10240, 1024), (7, 200, 224)])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
-def test_gemm_mx_matches_oracle(mx, M, N, K, out_dtype):
+def test_gemm_mx_matches_oracle(mx, M, N, K, mode, out_dtype):
     A, Bp, Bs = make_case(M, N, K, seed=M * 7 + N)
-    ref = o.ref_gemm_mx(A, Bp, Bs)
+    ref = o.ref_gemm_mx(A, Bp, Bs, MODES[mode])
     w = mx.prepack_mx(Bp, Bs)
-    C = mx.gemm_mx(torch.from_numpy(A).to(torch.bfloat16).cuda(), w, out_dtype=out_dtype)
+    C = mx.gemm_mx(torch.from_numpy(A).to(torch.bfloat16).cuda(), w, out_dtype=out_dtype, mode=mode)
     assert rel_err(C.float().cpu().numpy(), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("M", [1, 16, 4608])
+def test_gemm_split2_within_exact_bar(mx, M):
+    """split2 against the EXACT reference (bf16 activations, dequantised weights): the same
+    max|err|/max|ref| <= 1e-2 bar as the exact path."""
+    N, K = 3072, 3072
+    A, Bp, Bs = make_case(M, N, K, seed=5)
+    w = mx.prepack_mx(Bp, Bs)
+    C = mx.gemm_mx(torch.from_numpy(A).to(torch.bfloat16).cuda(), w, mode="split2").float().cpu().numpy()
+    rows = np.r_[0:min(M, 64), max(0, M - 64):M]
+    exact = A[rows] @ o.dequantize_mxfp4(Bp, Bs, axis=0)
+    assert rel_err(C[rows], exact) <= 1e-2
 
 
 def test_gemm_mx_flux_qkv_rows(mx):
