@@ -499,7 +499,10 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         int nb;
         long long end;
         gm_segment(s, s1, k_steps, nb, end);
-        if (!mbar_wait(&acc_empty[buf], ((eph >> buf) & 1) ^ 1, kErrWaitAccEmpty, abort_flag)) break;
+        if (!mbar_wait(&acc_empty[buf], ((eph >> buf) & 1) ^ 1, kErrWaitAccEmpty, abort_flag)) {
+          aborted = true;
+          break;
+        }
         eph ^= 1u << buf;
         tc_fence_after();
         for (const long long first = s; s < end; ++s) {
