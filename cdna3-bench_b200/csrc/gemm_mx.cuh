@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0, pend = 0, pend_ph = 0;
-      bool aborted = false;
+      bool aborted = false, coded = false;
       for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
         int mb, nb;
         tc_tile_coords(t, m_blocks, n_blocks, mb, nb);
@@ -217,10 +217,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], Cfg::kActBytes + Cfg::kWTxBytes + Cfg::kSfaBytes + Cfg::kSfbBytes);
-          tma_load_2d(smem + s * Cfg::kActBytes, &tm_act, &full[s], kt * kMxBK, mb * kMxTileB);
           tma_load_2d(smem + Cfg::kOffW + s * Cfg::kWBytes, &tm_w, &full[s], kt * kMxBK, nb * kTcTileW);
           bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes,
                     sfa + (static_cast<size_t>(nb) * k_steps + kt) * kMxSfBlock, Cfg::kSfaBytes, &full[s]);
+          if (!coded) {  // the codes come from the coder launched just before (PDL)
+            griddep_wait();
+            coded = true;
+          }
+          tma_load_2d(smem + s * Cfg::kActBytes, &tm_act, &full[s], kt * kMxBK, mb * kMxTileB);
           bulk_load(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes,
                     sfb + (static_cast<size_t>(kt) * sf_rows + 2 * mb) * kMxSfBlock, Cfg::kSfbBytes, &full[s]);
           pend |= 1u << s;
@@ -434,6 +438,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  griddep_launch_dependents();  // the bf16 conversion launched after this waits for it anyway
   const long long total = static_cast<long long>(n_blocks) * k_steps;
   const long long s0 = total * blockIdx.x / gridDim.x;
   const long long s1 = total * (blockIdx.x + 1) / gridDim.x;
@@ -466,6 +471,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     if (lane == 0) {
       int st = 0;
       uint32_t ph = 0, pend = 0, pend_ph = 0;
+      bool coded = false;
       for (long long s = s0; s < s1; ++s) {
         const int nb = static_cast<int>(s / k_steps), kt = static_cast<int>(s % k_steps);
         if (!mbar_wait(&empty[st], ph ^ 1, kErrWaitEmpty, abort_flag)) {
@@ -475,9 +481,13 @@ __global__ void __launch_bounds__(kGmThreads, 1)
         }
         mbar_arrive_expect_tx(&full[st], GmCfg::kWTxBytes + GmCfg::kBBytes + 2 * kMxSfBlock);
         tma_load_2d(smem + st * GmCfg::kWBytes, &tm_w, &full[st], kt * kMxBK, nb * kTcTileW);
-        tma_load_2d(smem + GmCfg::kOffB + st * GmCfg::kBBytes, &tm_b, &full[st], kt * kMxBK, 0);
         bulk_load(smem + GmCfg::kOffSfa + st * kMxSfBlock, sfa + (static_cast<size_t>(nb) * k_steps + kt) * kMxSfBlock,
                   kMxSfBlock, &full[st]);
+        if (!coded) {  // the codes come from the coder launched just before (PDL)
+          griddep_wait();
+          coded = true;
+        }
+        tma_load_2d(smem + GmCfg::kOffB + st * GmCfg::kBBytes, &tm_b, &full[st], kt * kMxBK, 0);
         bulk_load(smem + GmCfg::kOffSfb + st * kMxSfBlock, sfb + static_cast<size_t>(kt) * kMxSfBlock, kMxSfBlock,
                   &full[st]);
         pend |= 1u << st;
@@ -538,6 +548,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quarter: weight rows 32q .. 32q+31 of the block
+    griddep_wait();          // the coder has zeroed ws before the first atomic
     int buf = 0;
     uint32_t fph = 0;  // bit b: acc_full parity of buffer b
     for (long long s = s0; s < s1;) {
@@ -575,6 +586,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
 // fp32 [M][N] -> OutT [M][N] (the decode kernel's atomically summed result).
 __global__ void __launch_bounds__(256) mx_finalize_kernel(const float* __restrict__ ws, long long n,
                                                           __nv_bfloat16* __restrict__ C) {
+  griddep_wait();  // launched with PDL after the decode kernel: its atomics are complete
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n / 2;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float2 v = reinterpret_cast<const float2*>(ws)[i];
@@ -626,6 +638,7 @@ __global__ void __launch_bounds__(256) quant_act_mx8_kernel(const __nv_bfloat16*
                                                             int Kp, int G, int split, int rows_codes, int rows_sf,
                                                             uint8_t* __restrict__ codes, uint8_t* __restrict__ sfb,
                                                             float* __restrict__ zero_ws, long long zero_n) {
+  griddep_launch_dependents();  // the GEMM launched after this may start its weight loads
   const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   if (zero_ws)
     for (long long i = idx; i < zero_n / 4; i += static_cast<long long>(gridDim.x) * blockDim.x)

@@ -456,6 +456,24 @@ int code_act_mx8(const void* A, int M, int N, int K, int mode, uint8_t* dst, boo
   return launch_status();
 }
 
+// Launch with the programmatic-dependent-launch attribute: the kernel may start while the
+// launch before it in the stream (our own producer of its inputs) runs, and waits for that
+// launch with griddepcontrol.wait before it reads what the producer writes.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, int smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return ret(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 // 2-D map over 4-bit values [outer][inner] (rows of inner/2 bytes) that the TMA expands to
 // 16-byte units holding 8 bytes of data, the shared-memory form of an E2M1 kind::mxf8f6f4
 // operand.  inner is a multiple of 128 and the base 32-byte aligned.
@@ -496,11 +514,9 @@ int launch_mx(const uint8_t* codes, const uint8_t* wmx, void* C, int M, int N, i
                          static_cast<int>(sizeof(OutT)), C, N, M, static_cast<uint64_t>(N) * sizeof(OutT), 32, 32);
   if (rc) return rc;
   const int m_blocks = p.rows / kMxTileB, n_blocks = Np / kTcTileW;
-  const int grid = std::min(m_blocks * n_blocks, d->sm_count);
-  gemm_mx_kernel<OutT, kSplit><<<grid, kMxThreads, Cfg::kSmemBytes, stream>>>(
-      tm_act, tm_w, tm_out, wmx + mx_weight_data_bytes(N, K), codes + p.sf_off(), M, p.Kp / kMxBK, m_blocks,
-      n_blocks);
-  return launch_status();
+  return launch_pdl(gemm_mx_kernel<OutT, kSplit>, std::min(m_blocks * n_blocks, d->sm_count), kMxThreads,
+                    Cfg::kSmemBytes, stream, tm_act, tm_w, tm_out, wmx + mx_weight_data_bytes(N, K),
+                    codes + p.sf_off(), M, p.Kp / kMxBK, m_blocks, n_blocks);
 }
 
 // Decode (M <= 16): stream-K kernel into the zeroed fp32 buffer (C itself for fp32 output),
@@ -526,14 +542,13 @@ int launch_gemv_mx(const uint8_t* ws, const uint8_t* wmx, void* C, int c_dtype, 
   const int n_blocks = Np / kTcTileW, k_steps = p.Kp / kMxBK;
   const long long steps = static_cast<long long>(n_blocks) * k_steps;
   const int grid = static_cast<int>(std::min<long long>(d->sm_count, (steps + 3) / 4));  // >= 4 steps per CTA
-  gemv_mx_kernel<<<grid, kGmThreads, GmCfg::kSmemBytes, stream>>>(tm_w, tm_b, wmx + mx_weight_data_bytes(N, K),
-                                                                 ws + p.sf_off(), acc, M, N, n_blocks, k_steps);
-  rc = launch_status();
+  rc = launch_pdl(gemv_mx_kernel, grid, kGmThreads, GmCfg::kSmemBytes, stream, tm_w, tm_b,
+                  wmx + mx_weight_data_bytes(N, K), ws + p.sf_off(), acc, M, N, n_blocks, k_steps);
   if (rc || c_dtype == MXFP4_DTYPE_F32) return rc;
   const long long n = static_cast<long long>(M) * N;
   const int blocks = static_cast<int>(std::min<long long>((n / 2 + 255) / 256, 4LL * d->sm_count));
-  mx_finalize_kernel<<<blocks, 256, 0, stream>>>(acc, n, static_cast<__nv_bfloat16*>(C));
-  return launch_status();
+  return launch_pdl(mx_finalize_kernel, blocks, 256, 0, stream, static_cast<const float*>(acc), n,
+                    static_cast<__nv_bfloat16*>(C));
 }
 
 }  // namespace
