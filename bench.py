@@ -121,17 +121,35 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
-def cpu_sample(workload: str, gemm_ids, rows: int, seed: int = 0):
-    """Time the reference CPU algorithm (oracle port of ref.py ref_gemm) on `rows` activation
-    rows of each listed GEMM; returns (units, seconds) in the metric's unit base."""
-    import numpy as np
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
 
+    return platform.processor() or "unknown"
+
+
+def _oracle():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import mxfp4_ref as oracle
 
+    return oracle
+
+
+def cpu_inputs(workload: str, gemm_ids, rows: int, seed: int = 0):
+    """Seeded CPU inputs for `rows` activation rows of each listed GEMM of the workload:
+    [(A, B_packed, B_scales, units)] with units in the metric's base (FLOP or bytes)."""
+    import numpy as np
+
+    oracle = _oracle()
     M, gemms = shapes_for(workload, 1)
     rng = np.random.default_rng(seed)
-    units, secs = 0.0, 0.0
+    out = []
     for gi in gemm_ids:
         _, N, K = gemms[gi]
         m = min(rows, M)
@@ -139,12 +157,65 @@ def cpu_sample(workload: str, gemm_ids, rows: int, seed: int = 0):
         W = rng.standard_normal((K, N), dtype=np.float32) * np.float32(0.02)
         Bp, Bs = oracle.quantize_mxfp4_ocp(W, axis=0)
         del W
+        units = (N * K // 2 + N * K // 32 + m * K * 2) if is_decode(workload) else 2.0 * m * N * K
+        out.append((A, Bp, Bs, units))
+    return out
+
+
+def time_numpy_port(inputs) -> float:
+    """Seconds of the reference algorithm (oracle port of ref.py ref_gemm: NumPy dequant of the
+    full weights + fp32 BLAS matmul) over the inputs."""
+    oracle = _oracle()
+    secs = 0.0
+    for A, Bp, Bs, _ in inputs:
         t0 = time.perf_counter()
-        C = oracle.ref_gemm(A, Bp, Bs)
+        oracle.ref_gemm(A, Bp, Bs)
         secs += time.perf_counter() - t0
-        del C
-        units += (N * K // 2 + N * K // 32 + m * K * 2) if is_decode(workload) else 2.0 * m * N * K
-    return units, secs
+    return secs
+
+
+def time_torch_port(inputs) -> float:
+    """Seconds of the torch-CPU restatement: the same NumPy dequant, then torch.matmul in fp32."""
+    import torch
+
+    oracle = _oracle()
+    secs = 0.0
+    for A, Bp, Bs, _ in inputs:
+        t0 = time.perf_counter()
+        W = torch.from_numpy(oracle.dequantize_mxfp4(Bp, Bs, axis=0))
+        torch.matmul(torch.from_numpy(A), W)
+        secs += time.perf_counter() - t0
+    return secs
+
+
+def cpu_sample(workload: str, gemm_ids, rows: int, seed: int = 0):
+    """Time the reference CPU algorithm (oracle port of ref.py ref_gemm) on `rows` activation
+    rows of each listed GEMM; returns (units, seconds) in the metric's unit base."""
+    inputs = cpu_inputs(workload, gemm_ids, rows, seed)
+    return sum(u for *_, u in inputs), time_numpy_port(inputs)
+
+
+def cpu_baseline(workload: str, n_gemms: int, rows: int, reps: int = 3) -> dict:
+    """The CPU baseline of the JSON line: the NumPy port (the value) and the torch-CPU
+    restatement, each the median of `reps` timed repetitions on the same bounded sample."""
+    import statistics as st
+
+    import torch
+
+    unit = METRICS[workload][1]
+    scale = unit_scale(workload)
+    inputs = cpu_inputs(workload, list(range(n_gemms)), rows)
+    units = sum(u for *_, u in inputs)
+    t_np = st.median(time_numpy_port(inputs) for _ in range(reps))
+    t_torch = st.median(time_torch_port(inputs) for _ in range(reps))
+    M = shapes_for(workload, 1)[0]
+    return {"value": units / t_np / scale, "unit": unit, "cores": cpu_threads(), "kind": "port",
+            "sample": f"{min(rows, M)} activation rows of each GEMM of the step: NumPy dequant of the full "
+                      f"weights + fp32 BLAS matmul (oracle port of ref.py), median of {reps}",
+            "torch_cpu": {"value": units / t_torch / scale, "unit": unit, "threads": torch.get_num_threads(),
+                          "sample": "same sample: NumPy dequant + torch.matmul fp32, median of "
+                                    f"{reps}"},
+            "cpu_count": os.cpu_count(), "cpu_model": cpu_model()}
 
 
 def run_reference_arm(args, rank: int):
@@ -488,11 +559,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 4 * REF_SAMPLE_ROWS
-        u, s = cpu_sample(args.workload, list(range(len(items))), rows)
-        cpu = {"value": u / s / scale, "unit": unit, "cores": cpu_threads(), "kind": "port",
-               "sample": f"{min(rows, M)} activation rows of each GEMM of the step: NumPy dequant of "
-                         "the full weights + fp32 BLAS matmul (oracle port of ref.py)"}
+        cpu = cpu_baseline(args.workload, len(items), 4 * REF_SAMPLE_ROWS, reps=1 if decode else 3)
 
     if rank == 0:
         print(json.dumps({
