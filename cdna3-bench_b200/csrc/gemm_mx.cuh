@@ -46,7 +46,7 @@
 // Decode kernel (gemv_mx_kernel, M <= 16): stream-K over (128-row weight block, 128-k step)
 // pairs, one CTA per SM with an equal share; MMA N = 32 code rows; a CTA adds each finished
 // weight block's partial sums into an fp32 buffer with global atomics.
-// Every wait is bounded (common.cuh); no TMA multicast.
+// Every wait is bounded (common.cuh); every CTA loads its own tiles.
 #pragma once
 
 #include <cuda_fp16.h>
