@@ -79,3 +79,35 @@ def test_python_cost_model_agrees_with_library_path_choice(L):
     for M in (1, 2, 4, 8, 16, 17, 32, 64, 128, 256, 4608, 8192):
         for N, K in ((3072, 3072), (8192, 8192), (57344, 8192), (1024, 28672), (9216, 3072)):
             assert cm.pick_path(cm.Shape(M, N, K)) == names[L.lib().mxfp4_select_path(M, N, K)], (M, N, K)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 10240, 8192), (16, 200, 224), (17, 3072, 3072), (4608, 9216, 3072),
+                                   (300, 136, 96)])
+def test_block_scaled_sizes_match_layouts(L, M, N, K):
+    """Host arithmetic of the block-scaled path against the layouts the oracle restates."""
+    import mxfp4_ref as o
+    from mxfp4_b200 import kernels as kk
+
+    lib = L.lib()
+    Np, Kp = -(-N // 128) * 128, -(-K // 128) * 128
+    assert lib.mxfp4_mx_weight_bytes(N, K) == Np * Kp // 2 + Np * Kp // 32
+    for mode, name in ((o.MX_Q8, "q8"), (o.MX_SPLIT2, "split2")):
+        G, rows = o.mx_act_rows(M, mode)
+        assert kk.mx_code_rows(M, name) == rows
+        rows_sf = -(-rows // 128) * 128
+        codes = -(-(rows * Kp) // 256) * 256
+        sf = rows_sf * Kp // 32
+        acc = M * N * 4 if M <= 16 else 0
+        assert lib.mxfp4_mx_workspace_bytes(M, N, K, mode) == codes + (-(-sf // 256) * 256) + acc
+    assert lib.mxfp4_mx_workspace_bytes(M, N, K, 2) == 0  # unknown mode
+
+
+def test_block_scaled_rejects_bad_arguments(L):
+    lib = L.lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: argument checks fail first
+    assert lib.mxfp4_gemm_mx(p, p, p, L.DTYPE_BF16, 4, 128, 100, L.MX_Q8, p, 1 << 20, None) == 1001  # K % 32
+    assert lib.mxfp4_gemm_mx(p, p, p, L.DTYPE_BF16, 4, 100, 128, L.MX_Q8, p, 1 << 20, None) == 1001  # N % 8
+    assert lib.mxfp4_gemm_mx(p, p, p, L.DTYPE_BF16, 4, 128, 128, 7, p, 1 << 20, None) == 1000  # mode
+    assert lib.mxfp4_gemm_mx(p, p, p, L.DTYPE_BF16, 4, 128, 128, L.MX_Q8, p, 16, None) == 1003  # workspace
+    assert lib.mxfp4_prepack_mx(p, p, 128, 128, L.LAYOUT_G, p, None) == 1000  # layout
+    assert lib.mxfp4_quantize_act_mx8(p, 4, 100, L.MX_Q8, p, None) == 1001
