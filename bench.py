@@ -12,16 +12,22 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
 * value: whole-job TFLOP/s with inputs resident in HBM (prepacked weights), device-timed
   with CUDA events between barriers, max over ranks.  A step touches ~510 MB (> 126 MB L2),
   so each step's inputs have left L2 before the next step reads them.
-* e2e: the same metric through the one-call C-ABI entry (weights in the reference layout,
-  re-laid inside the call) with pinned HOST buffers: every step copies activations and
-  weights host->device and the bf16 outputs device->host inside the timed region.
+* e2e: the same metric through the one-call C-ABI entry mxfp4_gemm (kernels.gemm_packed:
+  reference-layout weights, re-laid inside the call into a preallocated workspace) from
+  pinned HOST buffers: every step copies activations and weights host->device and the bf16
+  outputs device->host inside the timed region.
 * roofline: the tensor-core kernel's achieved TFLOP/s (2*M*N*K per launch over its
   CUDA-event duration, events recorded inside the timed region) against the measured peak.
 * cpu_baseline: the reference algorithm (NumPy dequant + fp32 BLAS matmul, the oracle port
-  of ref.py:75-78) on a bounded sample of the workload, on this host's cores.
-* N > 1 (torchrun, NCCL): each rank owns its own N-slice of a w-times wider layer and runs
-  the same per-rank block (weak scaling, no collective on the data path); tp_sweep is the
-  strong-scaling column-parallel config with an NCCL all-gather of the output.
+  of ref.py:75-78) at the workload's full M, on this host's cores.
+* extra (N = 1, default workload only): the other measured workloads of the same library on
+  the same box -- the chained FLUX block (flux_chain) and the decode shapes at M = 1, 4, 16 --
+  each timed the same way with its own roofline fraction.
+* N > 1 (torchrun, NCCL): strong scaling of the same block, column-parallel: every GEMM's N is
+  split over the ranks in whole 128-row tiles and the all-gather is fused into the GEMM
+  epilogue (each output tile is stored into every GPU's full [M, N] output over NVLink), so
+  every GPU ends the step holding the whole block's outputs.  `--unfused` gives the baseline
+  (local GEMM, then an NCCL all-gather).  tp_sweep is BASELINE configs[4] in the same form.
 """
 
 from __future__ import annotations
@@ -38,14 +44,13 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "cdna3-bench_b200"))
 
 DECODE = [("qkv", 10240, 8192), ("o_proj", 8192, 8192), ("gate_up", 57344, 8192), ("down", 8192, 28672)]
+FLUX_DS = [("qkv", 9216, 3072), ("attn_out", 3072, 3072), ("mlp_up", 12288, 3072), ("mlp_down", 3072, 12288)]
 WORKLOADS = {
-    "flux_ds": (4608, [("qkv", 9216, 3072), ("attn_out", 3072, 3072), ("mlp_up", 12288, 3072),
-                       ("mlp_down", 3072, 12288)]),
+    "flux_ds": (4608, FLUX_DS),
     "flux_ss": (4608, [("qkv_mlp_up", 21504, 3072), ("out_mlp_down", 3072, 15360)]),
     # the double-stream block's linears chained as in the model (attention itself is out of scope:
     # the Q third of the QKV output stands in for its result), replayed from one CUDA graph
-    "flux_chain": (4608, [("qkv", 9216, 3072), ("attn_out", 3072, 3072), ("mlp_up", 12288, 3072),
-                          ("mlp_down", 3072, 12288)]),
+    "flux_chain": (4608, FLUX_DS),
     "c0": (128, [("c0", 3072, 3072)]),
     "decode_m1": (1, DECODE),
     "decode_m4": (4, DECODE),
@@ -62,10 +67,11 @@ METRICS = {
     "decode_m16": ("decode_m16_hbm_gbs", "GB/s"),
     "tp_sweep": ("tp_sweep_tflops", "TFLOP/s"),
 }
-REF_SAMPLE_ROWS = 256  # activation rows per GEMM in the CPU samples
+NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
+EXTRA_WORKLOADS = ("flux_chain", "decode_m1", "decode_m4", "decode_m16")
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -73,31 +79,19 @@ def parse():
     ap.add_argument("--workload", default="flux_ds", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the extra workloads of the default line")
     ap.add_argument("--mx", choices=["q8", "split2"], default=None,
                     help="block-scaled path (activations coded as E4M3 pieces, kind::mxf8f6f4 MMA; q8: one "
                          "OCP MXFP8 piece, split2: two pieces): one GPU, no e2e or CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--allgather", action="store_true", help="all-gather outputs (column-parallel)")
+    ap.add_argument("--weak", action="store_true",
+                    help="N > 1: each rank its own N-slice of a w-times wider layer, no collective (weak scaling)")
     ap.add_argument("--unfused", action="store_true",
-                    help="column-parallel: GEMM then a separate NCCL all-gather (default: all-gather fused "
-                         "into the GEMM epilogue, stores straight into every GPU's output over NVLink)")
+                    help="N > 1: GEMM then a separate NCCL all-gather (default: all-gather fused into the GEMM "
+                         "epilogue, stores straight into every GPU's output over NVLink)")
     ap.add_argument("--no-graph", action="store_true",
                     help="decode and c0 workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
-    return ap.parse_args()
-
-
-def shapes_for(workload: str, world: int):
-    M, gemms = WORKLOADS[workload]
-    if workload == "tp_sweep":  # strong scaling: the fixed layer is split column-wise
-        from mxfp4_b200.sharding import column_slice
-
-        rank = int(os.environ.get("RANK", "0"))
-        out = []
-        for n, N, K in gemms:
-            n0, n1 = column_slice(N, world, rank)
-            out.append((n, n1 - n0, K))
-        return M, out
-    return M, gemms
+    return ap.parse_args(argv)
 
 
 def is_decode(workload: str) -> bool:
@@ -108,7 +102,29 @@ def unit_scale(workload: str) -> float:
     return 1e9 if is_decode(workload) else 1e12  # GB/s or TFLOP/s
 
 
+def full_shapes(workload: str):
+    return WORKLOADS[workload]
+
+
 # ----------------------------------------------------------------------------- CPU side
+def use_all_host_threads() -> int:
+    """Let BLAS and torch use every host core (torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    try:
+        import torch
+
+        torch.set_num_threads(n)
+    except Exception:
+        pass
+    return n
+
+
 def cpu_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -141,108 +157,111 @@ def _oracle():
     return oracle
 
 
-def cpu_inputs(workload: str, gemm_ids, rows: int, seed: int = 0):
-    """Seeded CPU inputs for `rows` activation rows of each listed GEMM of the workload:
-    [(A, B_packed, B_scales, units)] with units in the metric's base (FLOP or bytes)."""
+def cpu_input(workload: str, gi: int, rows: int | None = None, seed: int = 0):
+    """Seeded CPU inputs of GEMM `gi` of the workload at `rows` activation rows (default: the
+    workload's full M): (A, B_packed, B_scales, units), units in the metric's base."""
     import numpy as np
 
     oracle = _oracle()
-    M, gemms = shapes_for(workload, 1)
-    rng = np.random.default_rng(seed)
-    out = []
-    for gi in gemm_ids:
-        _, N, K = gemms[gi]
-        m = min(rows, M)
-        A = rng.standard_normal((m, K), dtype=np.float32)
-        W = rng.standard_normal((K, N), dtype=np.float32) * np.float32(0.02)
-        Bp, Bs = oracle.quantize_mxfp4_ocp(W, axis=0)
-        del W
-        units = (N * K // 2 + N * K // 32 + m * K * 2) if is_decode(workload) else 2.0 * m * N * K
-        out.append((A, Bp, Bs, units))
-    return out
+    M, gemms = full_shapes(workload)
+    _, N, K = gemms[gi]
+    m = M if rows is None else min(rows, M)
+    rng = np.random.default_rng(seed + gi)
+    A = rng.standard_normal((m, K), dtype=np.float32)
+    W = rng.standard_normal((K, N), dtype=np.float32) * np.float32(0.02)
+    Bp, Bs = oracle.quantize_mxfp4_ocp(W, axis=0)
+    del W
+    units = (N * K // 2 + N * K // 32 + m * K * 2) if is_decode(workload) else 2.0 * m * N * K
+    return A, Bp, Bs, units
 
 
-def time_numpy_port(inputs) -> float:
-    """Seconds of the reference algorithm (oracle port of ref.py ref_gemm: NumPy dequant of the
-    full weights + fp32 BLAS matmul) over the inputs."""
+def time_numpy_port(inp) -> float:
+    """Seconds of one call of the reference algorithm (oracle port of ref.py ref_gemm: NumPy
+    dequant of the full weights + fp32 BLAS matmul)."""
     oracle = _oracle()
-    secs = 0.0
-    for A, Bp, Bs, _ in inputs:
-        t0 = time.perf_counter()
-        oracle.ref_gemm(A, Bp, Bs)
-        secs += time.perf_counter() - t0
-    return secs
+    A, Bp, Bs, _ = inp
+    t0 = time.perf_counter()
+    oracle.ref_gemm(A, Bp, Bs)
+    return time.perf_counter() - t0
 
 
-def time_torch_port(inputs) -> float:
+def time_torch_port(inp) -> float:
     """Seconds of the torch-CPU restatement: the same NumPy dequant, then torch.matmul in fp32."""
     import torch
 
     oracle = _oracle()
-    secs = 0.0
-    for A, Bp, Bs, _ in inputs:
-        t0 = time.perf_counter()
-        W = torch.from_numpy(oracle.dequantize_mxfp4(Bp, Bs, axis=0))
-        torch.matmul(torch.from_numpy(A), W)
-        secs += time.perf_counter() - t0
-    return secs
+    A, Bp, Bs, _ = inp
+    t0 = time.perf_counter()
+    W = torch.from_numpy(oracle.dequantize_mxfp4(Bp, Bs, axis=0))
+    torch.matmul(torch.from_numpy(A), W)
+    return time.perf_counter() - t0
 
 
-def cpu_sample(workload: str, gemm_ids, rows: int, seed: int = 0):
-    """Time the reference CPU algorithm (oracle port of ref.py ref_gemm) on `rows` activation
-    rows of each listed GEMM; returns (units, seconds) in the metric's unit base."""
-    inputs = cpu_inputs(workload, gemm_ids, rows, seed)
-    return sum(u for *_, u in inputs), time_numpy_port(inputs)
-
-
-def cpu_baseline(workload: str, n_gemms: int, rows: int, reps: int = 3) -> dict:
-    """The CPU baseline of the JSON line: the NumPy port (the value) and the torch-CPU
-    restatement, each the median of `reps` timed repetitions on the same bounded sample."""
-    import statistics as st
-
+def cpu_baseline(workload: str, reps: int = 1, rows: int | None = None, gemm_ids=None) -> dict:
+    """The CPU baseline of the JSON line: every GEMM of one step at the workload's full M (or
+    `rows` rows), the NumPy port (the value) and the torch-CPU restatement, each the median of
+    `reps` repetitions of the whole step."""
     import torch
 
+    use_all_host_threads()
     unit = METRICS[workload][1]
     scale = unit_scale(workload)
-    inputs = cpu_inputs(workload, list(range(n_gemms)), rows)
-    units = sum(u for *_, u in inputs)
-    t_np = st.median(time_numpy_port(inputs) for _ in range(reps))
-    t_torch = st.median(time_torch_port(inputs) for _ in range(reps))
-    M = shapes_for(workload, 1)[0]
-    return {"value": units / t_np / scale, "unit": unit, "cores": cpu_threads(), "kind": "port",
-            "sample": f"{min(rows, M)} activation rows of each GEMM of the step: NumPy dequant of the full "
-                      f"weights + fp32 BLAS matmul (oracle port of ref.py), median of {reps}",
-            "torch_cpu": {"value": units / t_torch / scale, "unit": unit, "threads": torch.get_num_threads(),
-                          "sample": "same sample: NumPy dequant + torch.matmul fp32, median of "
-                                    f"{reps}"},
+    M, gemms = full_shapes(workload)
+    ids = list(range(len(gemms))) if gemm_ids is None else list(gemm_ids)
+    t_np, t_torch, units = [], [], 0.0
+    inputs = [cpu_input(workload, gi, rows) for gi in ids]
+    units = sum(i[3] for i in inputs)
+    for _ in range(reps):
+        t_np.append(sum(time_numpy_port(i) for i in inputs))
+        t_torch.append(sum(time_torch_port(i) for i in inputs))
+    m = M if rows is None else min(rows, M)
+    return {"value": units / statistics.median(t_np) / scale, "unit": unit, "cores": cpu_threads(), "kind": "port",
+            "sample": f"every GEMM of one {workload} step at M = {m} (the workload's "
+                      f"{'full M' if m == M else 'first rows'}): NumPy dequant of the full weights + fp32 BLAS "
+                      f"matmul per GEMM (oracle port of ref.py ref_gemm), median of {reps}",
+            "torch_cpu": {"value": units / statistics.median(t_torch) / scale, "unit": unit,
+                          "threads": torch.get_num_threads(),
+                          "sample": f"same GEMMs: NumPy dequant + torch.matmul fp32, median of {reps}"},
             "cpu_count": os.cpu_count(), "cpu_model": cpu_model()}
 
 
 def run_reference_arm(args, rank: int):
-    """The reference's CPU implementation of the path (the oracle port: NumPy + BLAS with every
-    host thread) on the same config and metric, one bounded sample per step."""
+    """The reference's CPU implementation of the path (the oracle port of ref.py ref_gemm:
+    NumPy dequant + BLAS matmul with every host thread) on the same config and metric.  Each
+    step is one GEMM of the workload at its full M, round robin over the workload's GEMMs (the
+    dequant of that GEMM's weights happens inside the call, as in the reference).  Under
+    torchrun only rank 0 runs it."""
     if rank != 0:
         return
+    cores = use_all_host_threads()
     metric, unit = METRICS[args.workload]
-    n_gemm = len(shapes_for(args.workload, 1)[1])
+    M, gemms = full_shapes(args.workload)
+    inputs = {}
+
+    def inp(i):
+        gi = i % len(gemms)
+        if gi not in inputs:
+            inputs[gi] = cpu_input(args.workload, gi)
+        return inputs[gi]
+
     for i in range(args.warmup):
-        cpu_sample(args.workload, [i % n_gemm], REF_SAMPLE_ROWS, seed=i)
+        time_numpy_port(inp(i))
     units, secs = 0.0, 0.0
     for i in range(args.steps):
-        u, s = cpu_sample(args.workload, [i % n_gemm], REF_SAMPLE_ROWS, seed=100 + i)
-        units += u
-        secs += s
+        x = inp(i)
+        secs += time_numpy_port(x)
+        units += x[3]
     value = units / secs / unit_scale(args.workload)
-    M, gemms = shapes_for(args.workload, 1)
-    sample = (f"{REF_SAMPLE_ROWS} activation rows of one {args.workload} GEMM per step (round robin): "
-              "full NumPy dequant of that GEMM's weights + fp32 BLAS matmul")
+    sample = (f"one {args.workload} GEMM per step at the full M = {M} (round robin over {len(gemms)} GEMMs): "
+              "NumPy dequant of that GEMM's weights + fp32 BLAS matmul, as ref.py ref_gemm does per call")
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) OCP-MXFP4 weights)",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / max(1, args.steps) * 1e3,
+        "higher_is_better": True, "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) OCP-MXFP4 weights)",
         "config": {"workload": args.workload, "M": M, "gemms": gemms},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample,
+                         "cpu_model": cpu_model(), "blas_threads": cpu_threads()},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -254,11 +273,12 @@ class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int, period_s: float = 0.005):
+    def __init__(self, index: int, period_s: float = 0.001):
         self.index, self.period = index, period_s
         self.samples, self.reasons = [], 0
         self.max_mhz = None
         self._stop = threading.Event()
+        self._started = threading.Event()
         self._thr = None
         try:
             import pynvml
@@ -277,12 +297,14 @@ class ClockSampler:
                 self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
             except Exception:
                 pass
+            self._started.set()
             time.sleep(self.period)
 
     def __enter__(self):
         if self.nv is not None:
             self._thr = threading.Thread(target=self._run, daemon=True)
             self._thr.start()
+            self._started.wait(1.0)
         return self
 
     def __exit__(self, *exc):
@@ -308,71 +330,99 @@ def load_traffic(workload: str):
 
 
 # ----------------------------------------------------------------------------- GPU side
-def main():
-    args = parse()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        run_reference_arm(args, rank)
-        return
+class Ctx:
+    """Process-group facts and helpers shared by the measurements."""
 
-    import torch
-    import torch.distributed as dist
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
 
-    import mxfp4_b200 as mx
-    from mxfp4_b200 import kernels as kk
-    from mxfp4_b200 import cost_model
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", device_id=self.dev)
 
-    if not torch.cuda.is_available():
-        raise SystemExit("bench.py needs a CUDA device")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    metric, unit = METRICS[args.workload]
-    if args.mx:
-        if args.workload in ("flux_chain", "tp_sweep") or world > 1:
-            raise SystemExit("--mx: flux_ds, flux_ss, c0 or decode_* on one GPU")
-        metric, args.no_e2e, args.no_cpu_baseline = f"{metric}_mx_{args.mx}", True, True
-    M, gemms = shapes_for(args.workload, world)
-    decode = is_decode(args.workload)
-    scale = unit_scale(args.workload)
 
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)  # each rank: its own weight slice
+def tp_mode(args, ctx, workload: str) -> str:
+    """How the workload runs on this job: 'single' (one GPU), 'weak' (each rank its own slice of
+    a w-times wider layer), 'fused' / 'unfused' (column-parallel, all-gather fused or NCCL)."""
+    if ctx.world == 1:
+        return "single"
+    if args.weak and workload != "tp_sweep":
+        return "weak"
+    return "unfused" if args.unfused else "fused"
+
+
+def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -> dict:
+    """Time `steps` steps of `workload` (after `warmup`) and return the numbers of its line."""
+    import torch
+
+    import mxfp4_b200 as mx
+    from mxfp4_b200 import cost_model
+    from mxfp4_b200 import kernels as kk
+    from mxfp4_b200 import sharding
+
+    world, rank, dev = ctx.world, ctx.rank, ctx.dev
+    mode = tp_mode(args, ctx, workload)
+    M, full = full_shapes(workload)
+    decode = is_decode(workload)
+    scale = unit_scale(workload)
+    chain = workload == "flux_chain"
+    if chain and mode != "single":
+        raise SystemExit("flux_chain runs on one GPU")
+
+    # this rank's GEMMs: its column slice (tp), or the full layer (single / weak: every rank
+    # computes its own slice of a w-times wider layer, i.e. the full per-rank shape)
+    gemms = []
+    for name, N, K in full:
+        if mode in ("fused", "unfused"):
+            n0, n1 = sharding.column_slice(N, world, rank)
+            gemms.append((name, N, n0, n1 - n0, K))
+        else:
+            gemms.append((name, N, 0, N, K))
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     items = []
-    for name, N, K in gemms:
+    for name, N_full, n0, N, K in gemms:
         A = torch.randn((M, K), generator=gen, device=dev).to(torch.bfloat16)
         W = torch.randn((K, N), generator=gen, device=dev) * 0.02
         Bp, Bs = mx.quantize_mxfp4(W, axis=0, rule="ocp")
         del W
-        items.append({"name": name, "N": N, "K": K, "A": A, "Bp": Bp, "Bs": Bs,
+        items.append({"name": name, "N": N, "N_full": N_full, "n0": n0, "K": K, "A": A, "Bp": Bp, "Bs": Bs,
                       "w": mx.prepack_b200(Bp, Bs), "wmx": kk.prepack_mx(Bp, Bs) if args.mx else None,
                       "C": torch.empty((M, N), dtype=torch.bfloat16, device=dev)})
-    flops_step = sum(2.0 * M * it["N"] * it["K"] for it in items)
-    bytes_step = sum(cost_model.Shape(M, it["N"], it["K"]).in_bytes for it in items)
-    units_step = bytes_step if decode else flops_step
+    # work units of the whole job per step (strong scaling: the full layer once; otherwise each
+    # rank's own work, summed over ranks)
+    flops_rank = sum(2.0 * M * it["N"] * it["K"] for it in items)
+    bytes_rank = sum(cost_model.Shape(M, it["N"], it["K"]).in_bytes for it in items)
+    if mode in ("fused", "unfused"):
+        units_job = sum(cost_model.Shape(M, N, K).in_bytes if decode else 2.0 * M * N * K for _, N, K in full)
+    else:
+        units_job = world * (bytes_rank if decode else flops_rank)
 
     # decode and c0 weights fit in L2: rotate copies so the bytes between two reads of one copy
     # exceed L2 (c0's activations, 0.8 MB, stay resident as they would in a serving loop)
-    small = decode or args.workload == "c0"
+    small = decode or workload == "c0"
     rot = 1
     if small:
         l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-        rot = max(1, -(-3 * l2 // bytes_step))
+        rot = max(1, -(-3 * l2 // bytes_rank))
         for it in items:
             it["w_rot"] = [it["w"]] + [mx.MXFP4Weight(it["w"].data.clone(), it["w"].N, it["w"].K)
                                        for _ in range(rot - 1)]
@@ -386,88 +436,58 @@ def main():
             return kk.gemm_mx(it["A"], w, mode=args.mx, C=it["C"])
         return mx.gemm(it["A"], w, C=it["C"])
 
-    gather = fused = None
-    if world > 1 and (args.allgather or args.workload == "tp_sweep"):
-        from mxfp4_b200.sharding import all_gather_columns
-
-        full_n = [N for _, N, _ in WORKLOADS[args.workload][1]] if args.workload == "tp_sweep" \
-            else [world * it["N"] for it in items]
-        gather = lambda j, Y: all_gather_columns(Y, full_n[j])  # noqa: E731
-        fused = None
-        if not args.unfused:
-            from mxfp4_b200 import sharding
-
-            fused = [sharding.PeerOutput(M, full_n[j], torch.bfloat16) for j in range(len(items))]
-            offs = [sharding.column_slice(full_n[j], world, rank)[0] if args.workload == "tp_sweep"
-                    else rank * it["N"] for j, it in enumerate(items)]
-
+    peer = None
+    if mode == "fused":
+        peer = [sharding.PeerOutput(M, it["N_full"], torch.bfloat16) for it in items]
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
-          for _ in range(args.steps)]
+          for _ in range(steps)]
 
     def step(i_step: int, record: bool):
         for j, it in enumerate(items):
             w = it["w_rot"][i_step % rot] if small else (it["wmx"] if args.mx else it["w"])
             if record:
                 ev[i_step][j][0].record()
-            if fused is not None:
-                kk.gemm_allgather(it["A"], w, fused[j].ptrs, offs[j], fused[j].N)
+            if mode == "fused":
+                kk.gemm_allgather(it["A"], w, peer[j].ptrs, it["n0"], it["N_full"])
             else:
                 run_gemm(it, w)
             if record:
                 ev[i_step][j][1].record()
-            if fused is not None:
-                fused[j].sync()
-            elif gather is not None:
-                gather(j, it["C"])
+            if mode == "unfused":
+                sharding.all_gather_columns(it["C"], it["N_full"])
+        if mode == "fused":  # one stream-ordered collective: every peer's stores have landed
+            peer[-1].sync()
 
-    for i in range(args.warmup):
+    for i in range(warmup):
         step(i, False)
-    barrier()
+    ctx.barrier()
 
     # Decode and c0 GEMMs last ~5-60 us, about the host cost of a Python launch: a serving loop
     # replays them from a CUDA graph, and so does the bench (one graph per weight rotation,
     # with timing events recorded as graph nodes around every GEMM).
     graphs = None
-    chain = args.workload == "flux_chain"
     if chain:
         # h -> QKV -> (Q third as the attention stand-in) -> attn_out -> h + . -> MLP-up -> GELU
         # (tanh) -> MLP-down -> h + .   Only the four GEMMs count as work; the torch
         # element-wise ops between them are inside the timed graph.
-        import torch.nn.functional as F
+        from mxfp4_b200.flux import FluxChain
 
-        x0 = items[0]["A"]
-        attn_in = torch.empty((M, 3072), dtype=torch.bfloat16, device=dev)
-        h = torch.empty_like(x0)
-        out = torch.empty_like(x0)
+        fc = FluxChain([it["w"] for it in items], items[0]["A"])
         gev = [[(torch.cuda.Event(enable_timing=True, external=True),
                  torch.cuda.Event(enable_timing=True, external=True)) for _ in items]]
-
-        def chain_body():
-            def g(j, a):
-                gev[0][j][0].record()
-                y = mx.gemm(a, items[j]["w"], C=items[j]["C"])
-                gev[0][j][1].record()
-                return y
-
-            qkv = g(0, x0)
-            attn_in.copy_(qkv[:, :3072])
-            h.copy_(x0).add_(g(1, attn_in))
-            act = F.gelu(g(2, h), approximate="tanh")
-            torch.add(h, g(3, act), out=out)
-
         for _ in range(2):
-            chain_body()
+            fc.forward(gev[0])
         torch.cuda.synchronize()
         gch = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gch):
-            chain_body()
+            fc.forward(gev[0])
         graphs = [gch]
         gch.replay()
-        barrier()
+        ctx.barrier()
 
         def step(i_step: int, record: bool):  # noqa: F811
             gch.replay()
-    elif small and not args.no_graph and gather is None:
+    elif small and not args.no_graph and mode in ("single", "weak"):
         graphs, gev = [], []
         for r in range(rot):
             evs = [(torch.cuda.Event(enable_timing=True, external=True),
@@ -482,30 +502,31 @@ def main():
             gev.append(evs)
         for r in range(rot):
             graphs[r].replay()
-        barrier()
+        ctx.barrier()
 
         def step(i_step: int, record: bool):  # noqa: F811
             graphs[i_step % rot].replay()
 
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(ctx.local)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
-        barrier()
+        ctx.barrier()
         t0.record()
-        for i in range(args.steps):
+        for i in range(steps):
             step(i, True)
         t1.record()
-        barrier()
+        ctx.barrier()
     total_ms = t0.elapsed_time(t1)
     assert mx.device_error() == 0, "a kernel recorded a device error"
     if graphs is None:
-        launch_ms = [statistics.mean(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(args.steps))
+        launch_ms = [statistics.mean(ev[i][j][0].elapsed_time(ev[i][j][1]) for i in range(steps))
                      for j in range(len(items))]
     else:  # each graph's events hold its last replay inside the timed region
-        launch_ms = [statistics.mean(gev[r][j][0].elapsed_time(gev[r][j][1]) for r in range(min(len(gev), args.steps)))
+        launch_ms = [statistics.mean(gev[r][j][0].elapsed_time(gev[r][j][1]) for r in range(min(len(gev), steps)))
                      for j in range(len(items))]
-    ms_step = max_over_ranks(total_ms / args.steps)
-    value = world * units_step / (ms_step * 1e-3) / scale
+    ms_step = ctx.max_over_ranks(total_ms / steps)
+    launch_ms = [ctx.max_over_ranks(x) for x in launch_ms]
+    value = units_job / (ms_step * 1e-3) / scale
 
     peaks = cost_model.load_peaks()
     sustained = total_ms > 1000.0
@@ -519,85 +540,169 @@ def main():
                                 "roofline_us": rl.t_us, "frac_of_roofline": rl.t_us / (lm * 1e3),
                                 "bound": rl.bound}
     if decode:
-        ach = bytes_step / (sum(launch_ms) * 1e-3) / 1e9
+        ach = bytes_rank / (sum(launch_ms) * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": ach, "peak": peaks.hbm_gbs, "unit": "GB/s",
-                "frac": ach / peaks.hbm_gbs, "kernel": "gemv_kernel",
-                "peak_source": f"{peaks.source} hbm_gbs (copy)"}
-    elif args.mx and decode:
-        ach = bytes_step / (sum(launch_ms) * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": ach, "peak": peaks.hbm_gbs, "unit": "GB/s",
-                "frac": ach / peaks.hbm_gbs, "kernel": "quant_act_mx8_kernel + gemv_mx_kernel (+ finalize)",
+                "frac": ach / peaks.hbm_gbs,
+                "kernel": "quant_act_mx8_kernel + gemv_mx_kernel (+ finalize)" if args.mx else "gemv_kernel",
                 "peak_source": f"{peaks.source} hbm_gbs (copy)"}
     elif args.mx:  # 8-bit MMA: no fp8 GEMM is measured on this pool; its nominal rate is twice bf16
-        ach = flops_step / (sum(launch_ms) * 1e-3) / 1e12
+        ach = flops_rank / (sum(launch_ms) * 1e-3) / 1e12
         pk = 2.0 * (peaks.bf16_tflops_sustained if sustained else peaks.bf16_tflops)
         roof = {"bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
                 "kernel": "quant_act_mx8_kernel + gemm_mx_kernel",
                 "peak_source": f"2 x {peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16 "
                                "(the 8-bit MMA rate is twice the 16-bit one)"}
     else:
-        ach = flops_step / (sum(launch_ms) * 1e-3) / 1e12
+        ach = flops_rank / (sum(launch_ms) * 1e-3) / 1e12
         pk = peaks.bf16_tflops_sustained if sustained else peaks.bf16_tflops
         roof = {"bound": "tensor", "achieved": ach, "peak": pk, "unit": "TFLOP/s", "frac": ach / pk,
                 "kernel": "gemm_tc_kernel",
                 "peak_source": f"{peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16"}
-    roof["traffic"] = None if args.mx else load_traffic(args.workload)
-    if fused is not None:  # the fused GEMM + all-gather: compute or NVLink, whichever is slower
-        link_gbs = 770.0  # measured peer copy per direction on this pool's B200s
+    roof["traffic"] = None if (args.mx or mode != "single") else load_traffic(workload)
+    nvlink = None
+    if mode in ("fused", "unfused"):
+        # every GPU sends its slice of every output to each peer and receives the rest
         sent = sum(M * it["N"] * 2 * (world - 1) for it in items)
-        t_link = sent / (link_gbs * 1e9)
-        t_comp = flops_step / (peaks.bf16_tflops_sustained * 1e12)
-        if t_link > t_comp:
-            ach = sent / (sum(launch_ms) * 1e-3) / 1e9
-            roof = {"bound": "nvlink", "achieved": ach, "peak": link_gbs, "unit": "GB/s", "frac": ach / link_gbs,
-                    "kernel": "gemm_tc_kernel (all-gather epilogue)",
+        recv = sum(M * (N - it["N"]) * 2 for it, (_, N, _) in zip(items, full))
+        link = max(sent, recv)
+        t_link = link / (NVLINK_GBS * 1e9)
+        t_comp = flops_rank / ((peaks.bf16_tflops_sustained if sustained else peaks.bf16_tflops) * 1e12)
+        nvlink = {"bytes_sent_per_gpu": sent, "bytes_received_per_gpu": recv,
+                  "achieved_gbs": link / (ms_step * 1e-3) / 1e9, "peak_gbs": NVLINK_GBS,
+                  "frac": link / (ms_step * 1e-3) / 1e9 / NVLINK_GBS,
+                  "t_link_us": t_link * 1e6, "t_compute_us": t_comp * 1e6,
+                  "bound": "nvlink" if t_link > t_comp else "compute",
+                  "step_roofline_frac": max(t_link, t_comp) / (ms_step * 1e-3)}
+        if mode == "fused" and t_link > t_comp:
+            ach = link / (sum(launch_ms) * 1e-3) / 1e9
+            roof = {"bound": "nvlink", "achieved": ach, "peak": NVLINK_GBS, "unit": "GB/s",
+                    "frac": ach / NVLINK_GBS, "kernel": "gemm_tc_kernel (all-gather epilogue)",
                     "peak_source": "measured NVLink peer copy per direction", "traffic": None}
 
     e2e = None
-    if not args.no_e2e and args.workload not in ("tp_sweep", "flux_chain"):
-        e2e = run_e2e(args, mx, items, M, dev, units_step, scale, max_over_ranks, barrier, world)
+    if want_e2e and mode == "single" and not chain and not args.mx:
+        e2e = run_e2e(args, ctx, mx, items, M, units_job, scale, METRICS[workload][1], warmup, steps)
+
+    # our kernels per step: the GEMM, plus the decode activation prestage (4 <= M <= 16) or the
+    # split-K reduction (small M x N) where the workspace plan has them; the block-scaled path
+    # adds its activation coder (and, for decode, the bf16 conversion)
+    if args.mx:
+        per_step = len(items) * (3 if decode else 2)
+    elif mode == "fused":
+        per_step = len(items)
+    else:
+        per_step = sum(1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0 and M >= 4) for it in items)
+    launches = steps * per_step
+    return {"workload": workload, "mode": mode, "M": M, "items": items, "value": value, "ms_step": ms_step,
+            "per_gemm": per_gemm, "roofline": roof, "nvlink": nvlink, "e2e": e2e, "rot": rot, "small": small,
+            "graphs": graphs is not None, "chain": chain, "bytes_rank": bytes_rank, "launches": launches,
+            "clocks": sampler.summary(), "total_ms": total_ms}
+
+
+def parallelism_text(mode: str, world: int) -> str:
+    return {"single": "one GPU",
+            "weak": f"weak x{world}: each rank its own N-slice of a {world}x wider layer, no collective",
+            "fused": f"tp{world} column-parallel, all-gather fused into the GEMM epilogue (NVLink stores into every "
+                     "GPU's full output)",
+            "unfused": f"tp{world} column-parallel, local GEMM + NCCL all-gather"}[mode]
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import torch
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    ctx = Ctx()
+    metric, unit = METRICS[args.workload]
+    if args.mx:
+        if args.workload in ("flux_chain", "tp_sweep") or world > 1:
+            raise SystemExit("--mx: flux_ds, flux_ss, c0 or decode_* on one GPU")
+        metric, args.no_e2e, args.no_cpu_baseline = f"{metric}_mx_{args.mx}", True, True
+
+    r = measure(args, ctx, args.workload, args.steps, args.warmup, not args.no_e2e)
+    M = r["M"]
+    per_rank = [[it["name"], it["N"], it["K"]] for it in r["items"]]
+    out_bytes = sum(M * it["N"] * 2 for it in r["items"])
+
+    extra = None
+    if (world == 1 and args.workload == "flux_ds" and not args.mx and not args.no_extra):
+        extra = {}
+        for wl in EXTRA_WORKLOADS:
+            del_items(r)
+            x = measure(args, ctx, wl, min(args.steps, 20), max(3, args.warmup), False)
+            m, u = METRICS[wl]
+            extra[wl] = {"metric": m, "value": x["value"], "unit": u, "ms_per_step": x["ms_step"],
+                         "roofline_frac": x["roofline"]["frac"], "roofline_kernel": x["roofline"]["kernel"],
+                         "per_gemm": {k: {"us": v["us"], "frac_of_roofline": v["frac_of_roofline"],
+                                          "hbm_gbs" if is_decode(wl) else "tflops":
+                                          v["hbm_gbs"] if is_decode(wl) else v["tflops"]}
+                                      for k, v in x["per_gemm"].items()},
+                         "launch": "one CUDA graph per step", "clocks": x["clocks"],
+                         "l2": (f"{x['rot']} rotating weight copies (> 3x L2 per pass)" if x["small"]
+                                else "inputs larger than L2")}
+            del_items(x)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.workload, len(items), 4 * REF_SAMPLE_ROWS, reps=1 if decode else 3)
+        cpu = cpu_baseline(args.workload, reps=1)
 
     if rank == 0:
         print(json.dumps({
-            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong" if args.workload == "tp_sweep" else "weak", "vs_baseline": None,
+            "metric": metric, "value": r["value"], "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_step"], "higher_is_better": True,
+            "scaling": "strong" if r["mode"] in ("fused", "unfused") else "weak", "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 activations, N(0,0.02) OCP-MXFP4 weights)",
             "config": {
                 "workload": args.workload, "M": M,
-                "gemms": [[it["name"], it["N"], it["K"]] for it in items],
+                "gemms": [[n, N, K] for n, N, K in full_shapes(args.workload)[1]],
+                "gemms_per_rank": per_rank,
                 "weights": "MXFP4 (E2M1 + E8M0/32), prepacked, resident in HBM",
                 "activations": (f"coded inside each step as E4M3 pieces + E8M0/32 ({args.mx}), block-scaled MMA"
                                 if args.mx else "bf16"),
                 "output": "bf16", "accumulate": "fp32",
-                "l2": (f"{rot} rotating weight copies (> 3x L2 per pass)" if small
+                "l2": (f"{r['rot']} rotating weight copies (> 3x L2 per pass)" if r["small"]
                        else "inputs larger than L2: one step touches "
-                            f"{(bytes_step + sum(M * it['N'] * 2 for it in items)) / 1e6:.0f} MB"),
-                "launch": "one CUDA graph per step" if graphs is not None else "eager, one launch per GEMM",
+                            f"{(r['bytes_rank'] + out_bytes) / 1e6:.0f} MB per GPU"),
+                "launch": "one CUDA graph per step" if r["graphs"] else "eager, one launch per GEMM",
                 "chain": ("QKV -> Q third (attention stand-in) -> attn_out -> residual -> MLP-up -> GELU(tanh) "
-                          "-> MLP-down -> residual; torch element-wise ops inside the timed graph") if chain else None,
-                "parallelism": (f"tp{world} column-parallel, all-gather fused into the GEMM epilogue (NVLink "
-                                "stores into every GPU's output)" if fused is not None else
-                                f"tp{world} column-parallel + NCCL all-gather" if gather is not None
-                                else f"weak x{world}, per-rank N-slice, no collective"),
+                          "-> MLP-down -> residual; torch element-wise ops inside the timed graph") if r["chain"] else None,
+                "parallelism": parallelism_text(r["mode"], world),
             },
-            "roofline": roof, "per_gemm": per_gemm, "e2e": e2e, "cpu_baseline": cpu,
-            "gpu_launches": args.steps * sum((3 if decode else 2) if args.mx
-                                             else 1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0)
-                                             for it in items), "clocks": sampler.summary(),
+            "roofline": r["roofline"], "per_gemm": r["per_gemm"], "nvlink": r["nvlink"], "e2e": r["e2e"],
+            "cpu_baseline": cpu, "extra": extra, "gpu_launches": r["launches"], "clocks": r["clocks"],
         }), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        ctx.dist.destroy_process_group()
 
 
-def run_e2e(args, mx, items, M, dev, units_step, scale, max_over_ranks, barrier, world):
+def del_items(r: dict):
+    """Free a measurement's device buffers before the next one allocates its own."""
     import torch
 
+    r.get("items", []).clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def run_e2e(args, ctx, mx, items, M, units_step, scale, unit, warmup, steps):
+    """The same step through the public one-call entry (kernels.gemm_packed -> mxfp4_gemm with
+    the reference layout and a preallocated workspace) from pinned host buffers.  Per GEMM:
+    the weights and the activations go host->device, the GEMM re-lays the weights and
+    multiplies, the bf16 output comes back; the activations and outputs move in 256-row-tile
+    chunks on three streams (upload / compute / download) so the copies overlap the GEMMs."""
+    import torch
+
+    from mxfp4_b200 import kernels as kk
+
+    dev = ctx.dev
     h2d = d2h = 0
     host, devb = [], []
     for it in items:
@@ -609,15 +714,13 @@ def run_e2e(args, mx, items, M, dev, units_step, scale, max_over_ranks, barrier,
         hBs.copy_(it["Bs"])
         hC = torch.empty(it["C"].shape, dtype=it["C"].dtype, pin_memory=True)
         host.append((hA, hBp, hBs, hC))
-        ws = torch.empty(mx.workspace_bytes(M, it["N"], it["K"]), dtype=torch.uint8, device=dev)
+        ws = torch.empty(kk.workspace_bytes(M, it["N"], it["K"], "ref"), dtype=torch.uint8, device=dev)
         devb.append((torch.empty_like(it["A"]), torch.empty_like(it["Bp"]), torch.empty_like(it["Bs"]),
                      torch.empty_like(it["C"]), ws))
         h2d += hA.numel() * 2 + hBp.numel() + hBs.numel()
         d2h += hC.numel() * hC.element_size()
     s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-    # Row chunks of whole 256-row tiles: compute on chunk r overlaps the upload of chunk r+1 and
-    # the download of chunk r-1 (weights go first; they are re-laid once per GEMM).
     tiles = -(-M // 256)
     n_chunks = max(1, min(3, tiles))
     bounds = [min(M, (tiles * r // n_chunks) * 256) for r in range(n_chunks + 1)]
@@ -629,20 +732,17 @@ def run_e2e(args, mx, items, M, dev, units_step, scale, max_over_ranks, barrier,
             with torch.cuda.stream(s_in):
                 dBp.copy_(hBp, non_blocking=True)
                 dBs.copy_(hBs, non_blocking=True)
-                e_w = torch.cuda.Event()
-                e_w.record(s_in)
                 e_a = []
                 for r in range(n_chunks):
                     dA[bounds[r]:bounds[r + 1]].copy_(hA[bounds[r]:bounds[r + 1]], non_blocking=True)
                     e_a.append(torch.cuda.Event())
                     e_a[-1].record(s_in)
-            s_cmp.wait_event(e_w)
-            with torch.cuda.stream(s_cmp):
-                w = mx.prepack_b200(dBp, dBs)
             for r in range(n_chunks):
                 s_cmp.wait_event(e_a[r])
                 with torch.cuda.stream(s_cmp):
-                    mx.gemm(dA[bounds[r]:bounds[r + 1]], w, C=dC[bounds[r]:bounds[r + 1]])
+                    # one call: re-lay the reference-layout weights into the workspace and multiply
+                    kk.gemm_packed(dA[bounds[r]:bounds[r + 1]], dBp, dBs, C=dC[bounds[r]:bounds[r + 1]],
+                                   workspace=ws)
                     e_c = torch.cuda.Event()
                     e_c.record(s_cmp)
                 s_out.wait_event(e_c)
@@ -652,16 +752,17 @@ def run_e2e(args, mx, items, M, dev, units_step, scale, max_over_ranks, barrier,
         end.synchronize()  # the host reads the step's result
         return start.elapsed_time(end)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         e2e_step()
-    barrier()
-    n = max(3, min(args.steps, 20))
-    ms = max_over_ranks(statistics.mean(e2e_step() for _ in range(n)))
-    return {"value": world * units_step / (ms * 1e-3) / scale, "unit": METRICS[args.workload][1],
+    ctx.barrier()
+    n = max(3, min(steps, 20))
+    ms = ctx.max_over_ranks(statistics.mean(e2e_step() for _ in range(n)))
+    return {"value": units_step / (ms * 1e-3) / scale, "unit": unit,
             "ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": n,
-            "path": "public API from pinned host buffers: reference-layout weights uploaded and re-laid "
-                    "(prepack_b200) once per GEMM, activations uploaded, multiplied (gemm) and downloaded "
-                    "in 256-row-tile chunks, 3 streams (H2D / compute / D2H) overlapped"}
+            "path": "public one-call API kernels.gemm_packed (C ABI mxfp4_gemm, reference-layout weights re-laid "
+                    "inside each call into a preallocated workspace) from pinned host buffers: weights and "
+                    "activations uploaded, output downloaded every step, in 256-row-tile chunks on 3 streams "
+                    "(H2D / compute / D2H) overlapped"}
 
 
 if __name__ == "__main__":

@@ -59,7 +59,18 @@ __device__ unsigned int g_mxfp4_error;
 
 __device__ __forceinline__ void record_error(unsigned code) { atomicCAS(&g_mxfp4_error, 0u, code); }
 
-constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+constexpr unsigned long long kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s, the default limit
+
+// Limit of every bounded wait (kWaitLimitNs unless a test lowers it with mxfp4_test_hooks) and a
+// test switch that makes the weight producers of gemm_tc_kernel and gemv_kernel issue no copies,
+// so that their consumers' waits run out: the abort path is exercised without any fault.
+__device__ unsigned long long g_mxfp4_wait_limit_ns = kWaitLimitNs;
+__device__ int g_mxfp4_test_withhold;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *static_cast<volatile unsigned long long*>(&g_mxfp4_wait_limit_ns);
+}
+__device__ __forceinline__ bool test_withhold() { return *static_cast<volatile int*>(&g_mxfp4_test_withhold) != 0; }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -105,12 +116,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
+  const unsigned long long limit = wait_limit_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(a, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       record_error(code);
       *abort = 1;
       return false;
@@ -128,8 +140,9 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, unsign
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
   const unsigned long long t0 = globaltimer();
+  const unsigned long long limit = wait_limit_ns() / 4 + 1000000ull;
   while (!mbar_try_wait(a, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs / 4) {
+    if (globaltimer() - t0 > limit) {
       record_error(kErrWaitDrain);
       return;
     }

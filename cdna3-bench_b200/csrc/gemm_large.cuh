@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0, pend = 0, pend_ph = 0;
-      bool aborted = false;
+      bool aborted = test_withhold();  // test switch: issue nothing, the consumers' waits run out
       for (int t = blockIdx.x; t < total && !aborted; t += gridDim.x) {
         int mb, nb, kb_lo, kb_hi, ks;
         tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);

@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(kGvThreads, kGvMinBlocks)
       // for that launch to finish.
       const uint32_t xblk = 2u * M * 64;
       bool waited = false;
-      for (int i = 0; i < nst; ++i) {
+      const int n_issue = test_withhold() ? 0 : nst;  // test switch: issue nothing
+      for (int i = 0; i < n_issue; ++i) {
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {

@@ -222,6 +222,14 @@ int env_knob(const char* name) {
   return e ? std::atoi(e) : 0;
 }
 
+// Programmatic dependent launch between our own chained kernels is on unless MXFP4_NO_PDL=1
+// (read once per process): with it off every launch waits for the previous one in its stream,
+// which separates a kernel's own faults from the ordering of the chain when bringing one up.
+bool pdl_enabled() {
+  static const bool on = env_knob("MXFP4_NO_PDL") != 1;
+  return on;
+}
+
 // Decode plan: the K-split (cluster size) and ring depth.  Enough CTAs to fill every SM
 // twice and each CTA's K range at most 2048 (32 chunks) so the staged activations stay
 // small.  Two ring stages (35 KB): measured on B200, more resident CTAs (more compute warps
@@ -274,7 +282,7 @@ int launch_gemv_t(const void* A, const uint8_t* wpack, const OutSpec& o, int M, 
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = xpre ? 2 : 1;
+  cfg.numAttrs = xpre && pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_kernel<NT, OutT>, static_cast<const __nv_bfloat16*>(A), M, K,
                                      wpack, k_blocks_of(K), p.kbps, p.stages, out, N,
                                      xpre, xpre_shift);
@@ -334,7 +342,7 @@ int launch_gemv_tc_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // after our prestage kernel
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tc_kernel<OutT>, wpack, M, kb, kbps, xpre, xshift, out, N);
   return ret(e);
 }
@@ -470,7 +478,7 @@ int launch_pdl(void (*kernel)(KArgs...), int grid, int threads, int smem, cudaSt
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return ret(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
 }
 
@@ -593,6 +601,14 @@ int mxfp4_device_error(int clear, unsigned int* code_out) {
   }
   if (code_out) *code_out = v;
   return 0;
+}
+
+int mxfp4_test_hooks(int withhold, unsigned long long wait_limit_ns) {
+  const int w = withhold ? 1 : 0;
+  const unsigned long long lim = wait_limit_ns ? wait_limit_ns : kWaitLimitNs;
+  cudaError_t e = cudaMemcpyToSymbol(g_mxfp4_test_withhold, &w, sizeof(w));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mxfp4_wait_limit_ns, &lim, sizeof(lim));
+  return ret(e);
 }
 
 const char* mxfp4_error_string(int code) {

@@ -29,6 +29,7 @@ EXPORTED = (
     "mxfp4_device_info_get",
     "mxfp4_device_error",
     "mxfp4_error_string",
+    "mxfp4_test_hooks",
     "mxfp4_quantize",
     "mxfp4_dequantize",
     "mxfp4_prepacked_bytes",
@@ -83,6 +84,7 @@ def _declare(lib):
         "mxfp4_device_info_get": (_I, [_I, ctypes.POINTER(DeviceInfo)]),
         "mxfp4_device_error": (_I, [_I, ctypes.POINTER(ctypes.c_uint)]),
         "mxfp4_error_string": (ctypes.c_char_p, [_I]),
+        "mxfp4_test_hooks": (_I, [_I, ctypes.c_ulonglong]),
         "mxfp4_quantize": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
         "mxfp4_dequantize": (_I, [_P, _P, _I, _I, _I, _P, _I, _P]),
         "mxfp4_prepacked_bytes": (_SZ, [_I, _I]),

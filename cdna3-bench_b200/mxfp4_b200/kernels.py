@@ -336,15 +336,26 @@ def gemm_auto(A, B_packed, B_scales, C=None):
 
 
 def gemm_a(A, B_packed, B_scales, C=None):
-    """Two-pass path (the reference's strategy A, strategy_a_two_pass.cu): dequantise B to a
-    bf16 scratch matrix, then a library bf16 GEMM.  Kept as the unfused baseline."""
+    """Two-pass path (the reference's strategy A, strategy_a_two_pass.cu:39-116): dequantise B
+    exactly into a scratch matrix, then a library GEMM that accumulates and writes fp32.
+
+    The scratch holds the dequantised weights in fp32 and the GEMM runs in fp32 with TF32 off:
+    every product of a bf16 activation and a dequantised weight is exact in fp32, so C is the
+    fp32-accumulated product the reference's strategy A writes, not a bf16-rounded one.  Like
+    the reference it allocates its scratch on every call; it is the unfused baseline, not a
+    fast path."""
     M, N, K = _check_ref_inputs(A, B_packed, B_scales)
-    Bd = dequantize_mxfp4(B_packed, B_scales, axis=0, dtype=torch.bfloat16)
-    out = torch.matmul(A, Bd).float()
     if C is None:
-        return out
-    _check(C.dtype == torch.float32 and tuple(C.shape) == (M, N) and C.is_contiguous(), "C shape/contig")
-    C.copy_(out)
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    _check(C.is_cuda and C.dtype == torch.float32, "C must be float32")
+    _check(tuple(C.shape) == (M, N) and C.is_contiguous(), "C shape/contig")
+    Bd = dequantize_mxfp4(B_packed, B_scales, axis=0, dtype=torch.float32)  # [K, N], exact
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        torch.matmul(A.float(), Bd, out=C)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
     return C
 
 

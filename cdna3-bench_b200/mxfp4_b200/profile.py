@@ -2,7 +2,7 @@
 
     # run one entry point `--iters` times (wrap the command in ncu)
     python -m mxfp4_b200.profile one --path tc --M 4608 --N 9216 --K 3072
-    # summarise a launch list (ncu --metrics gpu__time_duration.sum --csv --log-file L.csv)
+    # summarise a launch list (ncu --metrics gpu__time_duration.sum --clock-control none --csv --log-file L.csv)
     python -m mxfp4_b200.profile launches L.csv
     # summarise a capture (ncu -i R.ncu-rep --page raw --csv > R.csv)
     python -m mxfp4_b200.profile raw R.csv

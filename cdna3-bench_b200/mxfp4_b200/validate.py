@@ -10,8 +10,11 @@ its entry point dispatches to.  On top of the reference's checks it runs each ke
 explicitly (tcgen05 large-M "tc", "tc_smem", decode "gemv"), the bf16-output entry point, and
 the bit-exact check of the dequantised tile the tensor cores consume.
 
-The reference product here is the library's exact GPU dequantiser followed by an fp32 torch
-matmul (ref_gemm), so the harness runs with the package alone.
+The reference product is computed on the CPU, as the reference's harness does with its
+rr.ref_gemm (validate.py:29-34): mxfp4_b200.ref dequantises the weight bytes in NumPy and
+multiplies in fp32 BLAS, with no GPU code involved, so a dequantisation bug shared by the
+kernels and the library's GPU dequantiser cannot pass unseen.  The bit-exact tile check also
+compares against that CPU dequantisation.
 """
 
 from __future__ import annotations
@@ -23,6 +26,7 @@ import numpy as np
 import torch
 
 from . import kernels as kk
+from . import ref as cpu_ref
 
 log = logging.getLogger("mxfp4_b200.validate")
 
@@ -43,7 +47,8 @@ def validate_shape(M: int, N: int, K: int, atol: float = 1e-2, rtol: float = 2e-
     A = torch.from_numpy(A_f32).to(torch.bfloat16).to(device)
     B_f32 = rng.standard_normal((K, N), dtype=np.float32) * 0.1
     B_packed, B_scales = kk.quantize_mxfp4(torch.from_numpy(B_f32).to(device), axis=0)
-    C_ref = kk.ref_gemm(A, B_packed, B_scales).cpu().numpy()
+    Bp_host, Bs_host = B_packed.cpu().numpy(), B_scales.cpu().numpy()
+    C_ref = cpu_ref.ref_gemm(A.float().cpu().numpy(), Bp_host, Bs_host)
 
     log.info("shape M=%d N=%d K=%d", M, N, K)
     all_ok = True
@@ -81,7 +86,7 @@ def validate_shape(M: int, N: int, K: int, atol: float = 1e-2, rtol: float = 2e-
     record("b200:bf16-out", lambda: kk.gemm(A, w, out_dtype=torch.bfloat16))
 
     tile = kk.dequantize_prepacked(w).float().cpu().numpy()  # [N, K]
-    ref_tile = kk.dequantize_mxfp4(B_packed, B_scales, axis=0).T.contiguous().cpu().numpy()
+    ref_tile = np.ascontiguousarray(cpu_ref.dequantize_ref_layout(Bp_host, Bs_host).T)
     exact = bool(np.array_equal(tile, ref_tile))
     log.info("  dequant tile bit-exact=%s", exact)
     all_ok = all_ok and exact

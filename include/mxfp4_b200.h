@@ -87,6 +87,15 @@ int mxfp4_device_error(int clear, unsigned int* code_out);
 
 const char* mxfp4_error_string(int code);
 
+/* Test hook (no counterpart in the reference, whose kernels have no bounded waits): sets, on
+ * the current device, the limit of every bounded wait inside the kernels (wait_limit_ns; 0
+ * restores the default of one second) and a switch that makes the weight producers of the
+ * large-M and decode kernels issue no copies (withhold != 0).  With the switch on, the
+ * consumers' waits run out after the limit, the kernel records a wait error readable with
+ * mxfp4_device_error(), releases its tensor memory and returns: the abort path runs without any
+ * fault.  Synchronous; for tests only -- turn the switch off again before real work. */
+int mxfp4_test_hooks(int withhold, unsigned long long wait_limit_ns);
+
 /* Quantise fp32 x[rows, cols] along `axis` (0: groups of 32 rows -> packed [rows/2, cols],
  * scales [rows/32, cols]; 1: groups of 32 columns -> [rows, cols/2], [rows, cols/32]).
  * Replaces quantize_mxfp4 (python/mxfp4_cdna3/ref.py:14-47) for rule MXFP4_RULE_REF. */

@@ -13,7 +13,7 @@ def test_cpu_baseline_fields():
     sys.path.insert(0, ROOT)
     import bench
 
-    cb = bench.cpu_baseline("c0", 1, 64, reps=2)
+    cb = bench.cpu_baseline("c0", reps=2, rows=64)
     assert cb["kind"] == "port" and cb["unit"] == "TFLOP/s" and cb["value"] > 0
     assert cb["torch_cpu"]["value"] > 0 and cb["torch_cpu"]["threads"] >= 1
     assert cb["cores"] >= 1 and cb["cpu_count"] >= 1 and isinstance(cb["cpu_model"], str)
@@ -26,3 +26,21 @@ def test_reference_arm_json_line():
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["metric"] == "c0_tflops" and line["value"] > 0
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["cpu_baseline"]["kind"] == "port"
+    # the reference arm times the workload's full M with every host thread
+    assert "M = 128" in line["cpu_baseline"]["sample"] and line["cpu_baseline"]["cores"] == os.cpu_count()
+
+
+def test_reference_arm_uses_all_threads_under_torchrun_env():
+    env = dict(os.environ, OMP_NUM_THREADS="1", WORLD_SIZE="2", RANK="0")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "c0",
+                        "--gpus", "2", "--steps", "1", "--warmup", "0"], capture_output=True, text=True,
+                       timeout=600, env=env)
+    assert r.returncode == 0, r.stderr
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["cpu_baseline"]["cores"] == os.cpu_count() and line["scaling"] == "strong"
+    # the other ranks print nothing and exit 0
+    env["RANK"] = "1"
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload", "c0",
+                        "--gpus", "2", "--steps", "1", "--warmup", "0"], capture_output=True, text=True,
+                       timeout=600, env=env)
+    assert r.returncode == 0 and r.stdout.strip() == ""

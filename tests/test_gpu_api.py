@@ -75,3 +75,18 @@ def test_device_info_and_predicates(mx):
     assert mx.shape_supported_c(4608, 9216, 3072)
     assert mx.select_path(4, 8192, 8192) == "gemv"
     assert mx.select_path(4608, 9216, 3072) == "tc"
+
+
+def test_gemm_a_writes_fp32_accumulated_product(mx):
+    """The unfused two-pass baseline writes the fp32-accumulated product like the reference's
+    strategy A: far tighter than the 2**-9 relative step a bf16-rounded result would show."""
+    M, N, K = 96, 640, 1024
+    A, Bp, Bs = make_case(M, N, K, seed=3)
+    ref = o.ref_gemm(A, Bp, Bs)
+    C = mx.gemm_a(torch.from_numpy(A).to(torch.bfloat16).cuda(), torch.from_numpy(Bp).cuda(),
+                  torch.from_numpy(Bs).cuda())
+    assert C.dtype == torch.float32
+    got = C.cpu().numpy()
+    assert rel_err(got, ref) < 1e-5
+    # a bf16-rounded output would miss the oracle by up to half a bf16 ulp of each element
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 0.05)) < 2.0 ** -12

@@ -3,12 +3,10 @@ cores' block-scaled MMA) against their oracle: byte-exact activation coding (bot
 weight re-layout, the GEMM within max|err|/max|ref| <= 1e-2 of (sum of the dequantised
 activation pieces) @ dequant(W), and the split2 mode within the same bar of the exact product.
 
-These tests run only with MXFP4_MX_GPU_TESTS=1: the path is built and its host logic is tested
-on CPU, but it has not yet had its first run on a B200, which is done deliberately, alone, on
-the smallest case before it joins the default GPU suite.
+The path's first GPU run followed a staged order (coder and prepack alone, then one small GEMM
+per kernel, then this whole file), with programmatic dependent launch off (MXFP4_NO_PDL=1) and
+then on; every stage passed, so these tests are part of the default GPU suite.
 """
-
-import os
 
 import numpy as np
 import pytest
@@ -17,11 +15,7 @@ import torch
 import mxfp4_ref as o
 from _util import make_case, rel_err
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("MXFP4_MX_GPU_TESTS") != "1",
-                       reason="block-scaled path: set MXFP4_MX_GPU_TESTS=1 to run its GPU tests"),
-]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.fixture(scope="module")

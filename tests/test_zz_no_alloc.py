@@ -3,8 +3,8 @@
 It exists for callers that cannot allocate device memory themselves (their device memory is
 owned by a custom allocator or pool, or allocating would synchronise a pipeline) and so
 cannot hand mxfp4_gemm a workspace for re-laying the weights.  These tests call it through
-the C ABI and compare it with mxfp4_gemm given a workspace, twice in a row, since every call
-reuses the library's one fixed buffer.  This file is collected last on purpose.
+the C ABI and compare it with mxfp4_gemm given a workspace and with the CPU oracle of the
+reference's ref_gemm, twice in a row, since every call reuses the library's one fixed buffer.  This file is collected last on purpose.
 """
 
 import ctypes
@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 import torch
 
+import mxfp4_ref as oracle
 from _util import make_case, rel_err
 
 TOL = 1e-2  # max|err| / max|ref|, as in the other GEMM tests
@@ -45,6 +46,7 @@ def test_noalloc_matches_workspace_entry_point_twice(M, N, K, layout):
     for call in range(2):  # the second call sees the first call's leftovers in the buffer
         A, Bp, Bs = make_case(M, N, K, seed=17 * call + M + N)
         At = torch.from_numpy(A).to(torch.bfloat16).cuda()
+        ref = oracle.ref_gemm(A, Bp, Bs)
         if layout == "nk":
             Bp, Bs = np.ascontiguousarray(Bp.T), np.ascontiguousarray(Bs.T)
         Bpt, Bst = torch.from_numpy(Bp).cuda(), torch.from_numpy(Bs).cuda()
@@ -58,3 +60,4 @@ def test_noalloc_matches_workspace_entry_point_twice(M, N, K, layout):
         w, g = want.cpu().numpy(), got.cpu().numpy()
         assert not np.isnan(g).any()
         assert rel_err(g, w) <= TOL
+        assert rel_err(g, ref) <= TOL  # and against the CPU oracle of the reference's ref_gemm
