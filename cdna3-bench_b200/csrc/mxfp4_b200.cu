@@ -14,6 +14,7 @@
 #include "gemm_large.cuh"
 #include "gemm_mx.cuh"
 #include "gemm_small.cuh"
+#include "gemm_small_sk.cuh"
 #include "gemm_small_tc.cuh"
 #include "quant.cuh"
 
@@ -36,6 +37,7 @@ struct DeviceState {
   std::atomic<bool> tc_attr[4] = {false, false, false, false};
   std::atomic<bool> gv_attr[4] = {false, false, false, false};
   std::atomic<bool> gt_attr[2] = {false, false};
+  std::atomic<bool> sk_attr[4] = {false, false, false, false};
   std::atomic<bool> mx_attr[4] = {false, false, false, false};
   std::atomic<bool> gm_attr{false};
 };
@@ -297,13 +299,76 @@ size_t gemv_prestage_bytes(int M, int N, int K) {
   return static_cast<size_t>(k_blocks_of(K)) * kGtXChunkBytes + 256;  // covers both kernels' layouts
 }
 
-// Which decode kernel runs when the activations can be prestaged: gemv_kernel (mma.sync) by
-// default; MXFP4_GEMV_KERNEL=2 selects gemv_tc_kernel (tcgen05).  Measured on B200, M = 1..16:
-// the tcgen05 kernel reaches 1.0-1.9 TB/s against 2.0-4.4 TB/s for gemv_kernel, so it is kept
-// as an alternative, not the default.
-bool gemv_use_tc() {
+// Which decode kernel runs when the caller's workspace has room: the persistent stream-K
+// gemv_sk_kernel by default; MXFP4_GEMV_KERNEL=1 selects the cluster split-K gemv_kernel and
+// MXFP4_GEMV_KERNEL=2 the tcgen05 gemv_tc_kernel (measured slower on B200: 1.0-1.9 TB/s), kept
+// as alternatives for comparison.
+int gemv_kernel_knob() {
   static const int knob = env_knob("MXFP4_GEMV_KERNEL");
-  return knob == 2;
+  return knob;
+}
+bool gemv_use_tc() { return gemv_kernel_knob() == 2; }
+
+// Workspace of the stream-K decode path (0 when M is outside its range).
+size_t gemv_sk_bytes(int M, int N, int K) {
+  if (M < 1 || M > 16) return 0;
+  return sk_workspace(M, n_blocks_of(N), k_blocks_of(K)).total;
+}
+
+template <int NT, typename OutT>
+int launch_gemv_sk_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K, const SkWorkspace& w,
+                     uint8_t* ws, cudaStream_t stream, DeviceState* d) {
+  const int slot = (NT == 1 ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
+  if (!d->sk_attr[slot]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_sk_kernel<NT, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         sk_smem_bytes(1) > sk_smem_bytes(16) ? sk_smem_bytes(1) : sk_smem_bytes(16));
+    if (e != cudaSuccess) return ret(e);
+    d->sk_attr[slot] = true;
+  }
+  GvOut<OutT> out;
+  std::memset(&out, 0, sizeof(out));
+  for (int i = 0; i < o.count; ++i) out.p[i] = static_cast<OutT*>(o.dst[i]);
+  out.count = o.count;
+  out.ldc = o.ldc;
+  out.n_off = o.n_off;
+  out.fence_sys = o.fence_sys;
+  const int nb = n_blocks_of(N), kb = k_blocks_of(K);
+  const long long units = static_cast<long long>(nb) * kb;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(d->sm_count, units)), 1, 1);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = sk_smem_bytes(M);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // after our prestage kernel
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_sk_kernel<NT, OutT>, wpack, M, N, kb, nb,
+                                     static_cast<const uint8_t*>(ws + w.x_off),
+                                     reinterpret_cast<const int*>(ws + w.shift_off),
+                                     reinterpret_cast<float*>(ws + w.acc_off), reinterpret_cast<int*>(ws + w.cnt_off),
+                                     out);
+  return ret(e);
+}
+
+// Stream-K decode: prestage (activations to f16, sums and counters zeroed), then the kernel.
+int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
+                   uint8_t* ws, cudaStream_t stream, DeviceState* d) {
+  const int nb = n_blocks_of(N), kb = k_blocks_of(K);
+  const SkWorkspace w = sk_workspace(M, nb, kb);
+  const long long zero_n4 = static_cast<long long>((w.total - w.acc_off) / 16);
+  const int grid = std::max(M, 2 * d->sm_count);
+  gemv_sk_prestage_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, kb, ws + w.x_off,
+                                                    reinterpret_cast<int*>(ws + w.shift_off),
+                                                    reinterpret_cast<float4*>(ws + w.acc_off), zero_n4);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return ret(e);
+  if (M <= 8)
+    return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_t<1, float>(wpack, C, M, N, K, w, ws, stream, d)
+                                      : launch_gemv_sk_t<1, __nv_bfloat16>(wpack, C, M, N, K, w, ws, stream, d);
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_t<2, float>(wpack, C, M, N, K, w, ws, stream, d)
+                                    : launch_gemv_sk_t<2, __nv_bfloat16>(wpack, C, M, N, K, w, ws, stream, d);
 }
 
 template <typename OutT>
@@ -349,6 +414,9 @@ int launch_gemv_tc_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K
 
 int launch_gemv(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
                 cudaStream_t stream, DeviceState* d, uint8_t* xws, size_t xws_bytes) {
+  const size_t sk_need = gemv_sk_bytes(M, N, K);
+  if (gemv_kernel_knob() == 0 && sk_need && xws && xws_bytes >= sk_need && (reinterpret_cast<uintptr_t>(xws) & 255) == 0)
+    return launch_gemv_sk(A, wpack, C, c_dtype, M, N, K, xws, stream, d);
   GvPlan p = plan_gemv(M, N, K, d->sm_count);
   const size_t need = gemv_prestage_bytes(M, N, K);
   uint8_t* xpre = nullptr;
@@ -724,7 +792,9 @@ int mxfp4_shape_supported(int path, int M, int N, int K) {
 size_t mxfp4_gemm_workspace_bytes(int M, int N, int K, int layout) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const size_t pre = layout == MXFP4_LAYOUT_PREPACKED ? 0 : (prepacked_bytes(N, K) + 255) / 256 * 256;
-  const size_t x = gemv_prestage_bytes(M, N, K);  // M <= 16: the decode path may serve the call
+  // M <= 16: the decode path may serve the call (stream-K workspace, or the prestaged activations of
+  // the other decode kernels)
+  const size_t x = std::max(gemv_prestage_bytes(M, N, K), gemv_sk_bytes(M, N, K));
   DeviceState* d = nullptr;
   const size_t sk = M > 16 && current_device(&d) == 0 ? splitk_bytes(M, N, K, d->sm_count) : 0;
   return pre + std::max(x, sk);

@@ -1,0 +1,61 @@
+"""CPU model of the stream-K decode kernel's schedule (gemv_sk_kernel in csrc/gemm_small_sk.cuh).
+
+The kernel gives CTA c the chunk range [c*U/G, (c+1)*U/G) of the U = n_blocks * k_blocks
+(row block, k-chunk) units, row-block-major; group q of its four chunk groups takes the CTA's
+chunks i = q (mod 4); at every row-block change and at the end each of the group's four warps
+adds the number of chunks it covered to the row block's counter, and the warp whose addition
+reaches 4 * k_blocks writes the row block.  This model replays that bookkeeping: every unit is
+processed exactly once, every row block's count reaches exactly 4 * k_blocks, exactly one warp
+finalises each row block, and it does so only after every chunk of the row block was covered.
+"""
+
+import itertools
+
+import pytest
+
+
+def replay(n_blocks, k_blocks, grid):
+    U = n_blocks * k_blocks
+    seen = [0] * U
+    events = []  # (row block, chunks) flushes, in an arbitrary but complete order
+    for c in range(grid):
+        u0, u1 = U * c // grid, U * (c + 1) // grid
+        for q in range(4):
+            seg_rb, seg_n = -1, 0
+            for i in range(q, u1 - u0, 4):
+                u = u0 + i
+                rb = u // k_blocks
+                if rb != seg_rb:
+                    if seg_rb >= 0:
+                        events += [(seg_rb, seg_n)] * 4  # the group's four warps
+                    seg_rb, seg_n = rb, 0
+                seen[u] += 1
+                seg_n += 1
+            if seg_rb >= 0:
+                events += [(seg_rb, seg_n)] * 4
+    return seen, events
+
+
+@pytest.mark.parametrize("n_blocks,k_blocks,grid", [
+    (80, 128, 148), (64, 128, 148), (448, 128, 148), (64, 448, 148),  # decode shapes (N/128, K/64)
+    (1, 1, 1), (1, 3, 1), (3, 5, 7), (2, 2, 148), (7, 13, 5), (5, 1, 3),
+])
+def test_every_unit_once_and_one_finaliser_per_row_block(n_blocks, k_blocks, grid):
+    grid = min(grid, n_blocks * k_blocks)
+    seen, events = replay(n_blocks, k_blocks, grid)
+    assert all(s == 1 for s in seen)
+    count = [0] * n_blocks
+    finalisers = [0] * n_blocks
+    for rb, n in events:
+        count[rb] += n
+        if count[rb] == 4 * k_blocks:
+            finalisers[rb] += 1
+    assert count == [4 * k_blocks] * n_blocks
+    assert finalisers == [1] * n_blocks
+
+
+def test_shares_differ_by_at_most_one_chunk():
+    for nb, kb, g in itertools.product((64, 80, 448), (128, 448), (148, 147)):
+        U = nb * kb
+        sizes = [U * (c + 1) // g - U * c // g for c in range(g)]
+        assert max(sizes) - min(sizes) <= 1
