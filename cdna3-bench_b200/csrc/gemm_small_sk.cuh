@@ -1,33 +1,33 @@
 // Small-M (decode, M <= 16) MXFP4 x BF16 GEMM, persistent stream-K form.
 //
-// Decode GEMMs are bound by streaming the packed weights from HBM once.  Two things keep a
-// streaming kernel below the HBM rate: too few bytes in flight per SM (each SM must cover the
-// DRAM latency with outstanding copies) and work that does not divide evenly into waves of CTAs
-// (a short weight matrix leaves most SMs idle in its last wave).  This kernel addresses both:
+// Decode GEMMs are bound by streaming the packed weights from HBM once.  What keeps a streaming
+// kernel below the HBM rate on B200: (1) the TMA engine of an SM handles a 1-D bulk copy at a
+// fixed cost of ~460 cycles up to ~16 KB (measured: 4 KB copies stream at 2.6 TB/s, 16 KB ones
+// at 6.9 TB/s, whatever the number in flight), so copies must be large; (2) work that does not
+// divide into whole waves of CTAs (a short weight matrix leaves most SMs idle in its last wave).
 //
 // * One CTA per SM, each streaming an equal, contiguous share of the (128-row weight block,
 //   64-k chunk) sequence in row-block-major order -- the shares differ by at most one chunk, so
 //   all SMs finish together whatever the shape.
-// * A producer warp keeps a ring of up to 64 one-chunk stages (~200 KB of shared memory) full
-//   with 1-D bulk copies: the chunk's 4352 bytes of weights plus its 128*M bytes of activations
-//   (f16, pre-scaled per row by a power of two so that every bf16 value is exact, staged once
-//   per GEMM by gemv_sk_prestage_kernel), so the whole ring is in flight from the start.
-// * 16 compute warps in 4 groups; group q takes the CTA's chunks i = q (mod 4) and each of its
+// * A producer warp keeps a ring of stages full, each stage kSkStageChunks consecutive chunks:
+//   one bulk copy of their weights (consecutive chunks are adjacent in memory, 17 KB) and one of
+//   their activation blocks (f16, 128*M bytes per chunk, pre-scaled per row by a power of two so
+//   that every bf16 value is exact, staged once per GEMM by gemv_sk_prestage_kernel).  The
+//   weights of the first ring-full of stages go out before the kernel waits for the prestage.
+// * 20 compute warps in 5 groups; group q takes the CTA's chunks i = q (mod 5) and each of its
 //   warps owns 32 weight rows (two m16 tiles) of the chunk.  Weights go through the hardware
 //   E2M1 -> f16 conversion (exact, unscaled) into mma.sync.m16n8k16 fragments with the
 //   activation rows as the n8 operand; each 32-element group's fp32 partial is multiplied by
-//   its E8M0 scale 2**(s-127) and accumulated in fp32 registers.
-// * Where a CTA's share ends inside a row block, several CTAs hold partial sums of it: at the
-//   end of each row-block segment every warp adds its partial sums into an fp32 buffer in
-//   workspace (zeroed by the prestage kernel) with global reductions, fences, and adds the
-//   number of chunks it covered to the row block's counter.  The warp whose addition completes
-//   the count (4 warps x k_blocks chunks) converts the row block's 128 x M sums to the output
-//   (undoing the activation row shifts) and writes it to every destination.  No warp waits
-//   for another one: there is no inter-CTA barrier and no named barrier, so a wait that gives
-//   up cannot strand anybody.
-// * The launch carries the programmatic-dependent-launch attribute: it starts while the
-//   prestage kernel runs, issues its first weight copies and waits (griddepcontrol.wait) only
-//   before it touches the activations, the sums or the counters.
+//   its E8M0 scale 2**(s-127) and accumulated in fp32 registers.  Ring positions and row-block
+//   and k indices advance incrementally: no integer division in the streaming loops.
+// * At the end of each row-block segment every warp adds its partial sums into an fp32 buffer
+//   in workspace (zeroed by the prestage kernel) with global reductions: several CTAs (and the
+//   five groups of one CTA) hold parts of a row block.  No warp waits for another one: there is
+//   no inter-CTA barrier and no named barrier, so a wait that gives up strands nobody.
+// * gemv_sk_finalize_kernel turns the sums into the output (undoing the activation row shifts),
+//   for every destination.
+// * The three launches are chained with programmatic dependent launch: each starts while the one
+//   before runs and waits (griddepcontrol.wait) only before it reads that one's results.
 #pragma once
 
 #include "common.cuh"
@@ -35,16 +35,26 @@
 
 namespace mxb {
 
-constexpr int kSkGroups = 4;                     // chunk groups (chunks i = q mod 4)
+#ifndef MXFP4_SK_DIAG
+#define MXFP4_SK_DIAG 0  // sweep-only: 1 = consumers skip the arithmetic, 2 = the producer issues nothing
+                         // and the consumers do not wait for it (compute rate alone), 8 = no global
+                         // reductions; results are wrong in these builds
+#endif
+
+constexpr int kSkGroups = 5;                     // chunk groups (chunks i = q mod 5)
 constexpr int kSkComputeWarps = 4 * kSkGroups;   // each group: 4 warps x 32 weight rows
-constexpr int kSkThreads = 32 * (kSkComputeWarps + 1);  // + 1 producer warp = 544
+constexpr int kSkThreads = 32 * (kSkComputeWarps + 1);  // + 1 producer warp = 672
+#ifndef MXFP4_SK_STAGE_CHUNKS
+#define MXFP4_SK_STAGE_CHUNKS 4
+#endif
+constexpr int kSkStageChunks = MXFP4_SK_STAGE_CHUNKS;  // consecutive chunks per ring stage
 constexpr int kSkMaxStages = 64;
 constexpr int kSkRingBytes = 200 * 1024;
 
 // Host and device agree on the ring from these.
-__host__ __device__ constexpr int sk_stage_bytes(int M) { return kChunkBytes + 128 * M; }
+__host__ __device__ constexpr int sk_stage_bytes(int M) { return kSkStageChunks * (kChunkBytes + 128 * M); }
 __host__ __device__ constexpr int sk_stages(int M) {
-  return (kSkRingBytes / sk_stage_bytes(M) < kSkMaxStages ? kSkRingBytes / sk_stage_bytes(M) : kSkMaxStages) & ~3;
+  return kSkRingBytes / sk_stage_bytes(M) < kSkMaxStages ? kSkRingBytes / sk_stage_bytes(M) : kSkMaxStages;
 }
 __host__ __device__ constexpr int sk_off_bar(int M) { return sk_stages(M) * sk_stage_bytes(M); }
 __host__ __device__ constexpr int sk_smem_bytes(int M) { return sk_off_bar(M) + 2 * kSkMaxStages * 8 + 16; }
@@ -52,10 +62,9 @@ __host__ __device__ constexpr int sk_smem_bytes(int M) { return sk_off_bar(M) + 
 // Workspace of the stream-K decode path, carved in this order (each part 256-byte aligned):
 //   activations f16, k_blocks * 128 * M bytes (gemv_prestage_kernel's layout);
 //   row shifts int[16];
-//   fp32 sums [M][n_blocks * 128];
-//   chunk counters int[n_blocks].
+//   fp32 sums [M][n_blocks * 128].
 struct SkWorkspace {
-  size_t x_off, shift_off, acc_off, cnt_off, total;
+  size_t x_off, shift_off, acc_off, total;
 };
 __host__ __device__ inline size_t sk_align(size_t x) { return (x + 255) / 256 * 256; }
 __host__ __device__ inline SkWorkspace sk_workspace(int M, int n_blocks, int k_blocks) {
@@ -63,8 +72,7 @@ __host__ __device__ inline SkWorkspace sk_workspace(int M, int n_blocks, int k_b
   w.x_off = 0;
   w.shift_off = sk_align(static_cast<size_t>(k_blocks) * 128 * M);
   w.acc_off = w.shift_off + 256;
-  w.cnt_off = w.acc_off + sk_align(static_cast<size_t>(M) * n_blocks * kChunkRows * 4);
-  w.total = w.cnt_off + sk_align(static_cast<size_t>(n_blocks) * 4);
+  w.total = w.acc_off + sk_align(static_cast<size_t>(M) * n_blocks * kChunkRows * 4);
   return w;
 }
 
@@ -72,40 +80,53 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
   asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
-// Activations to f16 for the stream-K kernel, and the zeroing of its sums and counters.
-// Blocks b < M stage activation row b exactly as gemv_prestage_kernel does; every block also
-// zeroes its share of the fp32 sums and chunk counters.  The dependent decode launch may start
-// as soon as every block here has begun.
-__global__ void __launch_bounds__(256) gemv_sk_prestage_kernel(const __nv_bfloat16* __restrict__ A, int M, int K,
-                                                               int k_blocks, uint8_t* __restrict__ xpre,
-                                                               int* __restrict__ xshift, float4* __restrict__ zero,
-                                                               long long zero_n4) {
+constexpr int kSkPreThreads = 1024;
+constexpr int kSkPreVecs = 4;  // 16-byte vectors of a row each prestage thread holds (K <= 32768)
+
+// Activations to f16 for the stream-K kernel, and the zeroing of its fp32 sums.  Blocks b < M
+// stage activation row b in the layout gemv_prestage_kernel writes: each thread loads its
+// (up to four) 16-byte vectors of the row once, the block reduces the row's max |x| to a power-
+// of-two shift that puts it in [2^14, 2^15), and the same registers are converted and stored --
+// two memory round trips per row.  Every block also zeroes a share of the sums.  The dependent
+// decode launch may start as soon as every block here has begun.
+__global__ void __launch_bounds__(kSkPreThreads) gemv_sk_prestage_kernel(const __nv_bfloat16* __restrict__ A, int M,
+                                                                         int K, int k_blocks,
+                                                                         uint8_t* __restrict__ xpre,
+                                                                         int* __restrict__ xshift,
+                                                                         float4* __restrict__ zero, long long zero_n4) {
   griddep_launch_dependents();
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < zero_n4; i += static_cast<long long>(gridDim.x) * 256)
+  for (long long i = blockIdx.x * static_cast<long long>(kSkPreThreads) + threadIdx.x; i < zero_n4;
+       i += static_cast<long long>(gridDim.x) * kSkPreThreads)
     zero[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   const int m = blockIdx.x;
   if (m >= M) return;
-  __shared__ float wmax[8];
+  __shared__ float wmax[kSkPreThreads / 32];
   const int nvec = k_blocks * 8;
   const __nv_bfloat16* arow = A + static_cast<size_t>(m) * K;
+  uint4 raw[kSkPreVecs];
   float amax = 0.0f;
-  for (int v = threadIdx.x; v < nvec; v += 256)
-    if (v * 8 < K) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(arow + v * 8);
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        amax = fmaxf(amax, fabsf(__uint_as_float(w[i] << 16)));
-        amax = fmaxf(amax, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
-      }
+  for (int j = 0; j < kSkPreVecs; ++j) {
+    const int v = threadIdx.x + j * kSkPreThreads;
+    raw[j] = make_uint4(0, 0, 0, 0);
+    if (v < nvec && v * 8 < K) raw[j] = *reinterpret_cast<const uint4*>(arow + v * 8);
+  }
+#pragma unroll
+  for (int j = 0; j < kSkPreVecs; ++j) {
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      amax = fmaxf(amax, fabsf(__uint_as_float(w[i] << 16)));
+      amax = fmaxf(amax, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
     }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, wmax[i]);
+  for (int i = 0; i < kSkPreThreads / 32; ++i) amax = fmaxf(amax, wmax[i]);
   int shift = 0;
   if (amax > 0.0f && amax <= 3.0e38f) {
     int E;
@@ -114,10 +135,11 @@ __global__ void __launch_bounds__(256) gemv_sk_prestage_kernel(const __nv_bfloat
   }
   if (threadIdx.x == 0) xshift[m] = shift;
   const float f1 = exp2i(shift / 2), f2 = exp2i(shift - shift / 2);
-  for (int v = threadIdx.x; v < nvec; v += 256) {
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (v * 8 < K) raw = *reinterpret_cast<const uint4*>(arow + v * 8);
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int j = 0; j < kSkPreVecs; ++j) {
+    const int v = threadIdx.x + j * kSkPreThreads;
+    if (v >= nvec) break;
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
     const int kg = v >> 2, slot = v & 3;
     uint32_t* blk = reinterpret_cast<uint32_t*>(xpre) + (static_cast<size_t>(kg) * M + m) * 16 + slot;
 #pragma unroll
@@ -129,11 +151,10 @@ __global__ void __launch_bounds__(256) gemv_sk_prestage_kernel(const __nv_bfloat
   }
 }
 
-template <int NT, typename OutT>
+template <int NT>
 __global__ void __launch_bounds__(kSkThreads, 1)
-    gemv_sk_kernel(const uint8_t* __restrict__ wpack, int M, int N, int k_blocks, int n_blocks,
-                   const uint8_t* __restrict__ xpre, const int* __restrict__ xshift, float* __restrict__ acc,
-                   int* __restrict__ cnt, const GvOut<OutT> out) {
+    gemv_sk_kernel(const uint8_t* __restrict__ wpack, int M, int k_blocks, int n_blocks,
+                   const uint8_t* __restrict__ xpre, float* __restrict__ acc) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int stages = sk_stages(M);
   const int sbytes = sk_stage_bytes(M);
@@ -150,38 +171,64 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 4);  // the four warps of the stage's group
+      mbar_init(&empty[i], 4 * kSkStageChunks);  // each chunk's four warps
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_launch_dependents();  // the finalize launch waits for this grid anyway
 
   if (warp == kSkComputeWarps) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint64_t pend = 0, pend_ph = 0;
-      bool aborted = false, waited = false;
-      const int n_issue = test_withhold() ? 0 : n_my;  // test switch: issue nothing
-      for (int i = 0; i < n_issue; ++i) {
-        const int s = i % stages;
-        const uint32_t ph = (i / stages) & 1;
+      bool aborted = false;
+      const int n_issue = (test_withhold() || (MXFP4_SK_DIAG & 2)) ? 0 : n_my;  // test switch: issue nothing
+      // Stage, its phase parity and the next activation block's k index advance without
+      // divisions.  The weights of the first `stages` stages go out before the wait for the
+      // prestage launch (they do not depend on it); their activation blocks follow it.
+      const int nst = (n_issue + kSkStageChunks - 1) / kSkStageChunks;
+      const int first = min(stages, nst);
+      int kc = static_cast<int>(u0 % k_blocks);
+      const uint8_t* wsrc = wpack + u0 * kChunkBytes;
+      auto issue_x = [&](int j, int nch) {  // the stage's activation blocks, one copy per k run
+        uint8_t* xdst = smem + j * sbytes + kSkStageChunks * kChunkBytes;
+        for (int c = 0; c < nch;) {
+          const int run = min(nch - c, k_blocks - kc);
+          bulk_load(xdst + c * xbytes, xpre + static_cast<size_t>(kc) * xbytes, run * xbytes, &full[j]);
+          c += run;
+          kc += run;
+          if (kc == k_blocks) kc = 0;
+        }
+      };
+      for (int j = 0; j < first; ++j) {
+        const int nch = min(kSkStageChunks, n_issue - j * kSkStageChunks);
+        mbar_arrive_expect_tx(&full[j], nch * (kChunkBytes + xbytes));
+        bulk_load(smem + j * sbytes, wsrc, nch * kChunkBytes, &full[j]);
+        wsrc += nch * kChunkBytes;
+        pend |= 1ull << j;
+      }
+      if (first > 0) griddep_wait();  // the activations come from the prestage launch before this one
+      for (int j = 0; j < first; ++j) issue_x(j, min(kSkStageChunks, n_issue - j * kSkStageChunks));
+      int s = first == stages ? 0 : first;
+      uint32_t ph = first == stages ? 1 : 0;
+      for (int j = first; j < nst; ++j) {
         if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
           aborted = true;
           break;
         }
-        const long long u = u0 + i;
-        const int kc = static_cast<int>(u % k_blocks);
-        uint8_t* st = smem + s * sbytes;
-        mbar_arrive_expect_tx(&full[s], kChunkBytes + xbytes);
-        bulk_load(st, wpack + u * kChunkBytes, kChunkBytes, &full[s]);
-        if (!waited) {  // the activations come from the prestage launch just before this one
-          griddep_wait();
-          waited = true;
-        }
-        bulk_load(st + kChunkBytes, xpre + static_cast<size_t>(kc) * xbytes, xbytes, &full[s]);
+        const int nch = min(kSkStageChunks, n_issue - j * kSkStageChunks);
+        mbar_arrive_expect_tx(&full[s], nch * (kChunkBytes + xbytes));
+        bulk_load(smem + s * sbytes, wsrc, nch * kChunkBytes, &full[s]);
+        issue_x(s, nch);
         pend |= 1ull << s;
         pend_ph = (pend_ph & ~(1ull << s)) | (static_cast<uint64_t>(ph) << s);
+        wsrc += nch * kChunkBytes;
+        if (++s == stages) {
+          s = 0;
+          ph ^= 1;
+        }
       }
       if (aborted)  // let every copy we started land before the CTA can exit
         for (int i = 0; i < stages; ++i)
@@ -191,7 +238,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   }
 
   // -------------------------------------------------------------- compute warps
-  griddep_wait();  // sums and counters zeroed, row shifts written
+  griddep_wait();  // the sums are zeroed
   const int q = warp >> 2;   // chunk group
   const int wq = warp & 3;   // rows 32*wq .. 32*wq+31 of every chunk
   const int g = lane >> 2, t = lane & 3;
@@ -216,109 +263,131 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 #pragma unroll
     for (int j = 0; j < NT; ++j) accr[a][j][0] = accr[a][j][1] = accr[a][j][2] = accr[a][j][3] = 0.0f;
 
-  // Adds this warp's partial sums of row block rb (covering nch chunks) into the fp32 sums and
-  // the row block's counter; the warp that completes the count writes the row block's output.
-  auto flush = [&](int rb, int nch) {
+  // Adds this warp's partial sums of row block rb into the fp32 sums and clears them.
+  auto flush = [&](int rb) {
 #pragma unroll
     for (int a = 0; a < 2; ++a)
 #pragma unroll
       for (int jt = 0; jt < NT; ++jt) {
         const int n = rb * kChunkRows + 32 * wq + 16 * a + g;
         const int m = 8 * jt + 2 * t;
-        if (m < M) {
+        if ((MXFP4_SK_DIAG & 8) == 0 && m < M) {
           red_add_f32(acc + static_cast<size_t>(m) * Np + n, accr[a][jt][0]);
           red_add_f32(acc + static_cast<size_t>(m) * Np + n + 8, accr[a][jt][2]);
         }
-        if (m + 1 < M) {
+        if ((MXFP4_SK_DIAG & 8) == 0 && m + 1 < M) {
           red_add_f32(acc + static_cast<size_t>(m + 1) * Np + n, accr[a][jt][1]);
           red_add_f32(acc + static_cast<size_t>(m + 1) * Np + n + 8, accr[a][jt][3]);
         }
         accr[a][jt][0] = accr[a][jt][1] = accr[a][jt][2] = accr[a][jt][3] = 0.0f;
       }
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(cnt + rb, nch) + nch == 4 * k_blocks;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    for (int m = 0; m < M; ++m) {
-      const int sh = __ldcg(xshift + m);
-#pragma unroll
-      for (int r = lane; r < kChunkRows; r += 32) {
-        const int n = rb * kChunkRows + r;
-        if (n < N) {
-          const OutT v = gv_out<OutT>(ldexpf(__ldcg(acc + static_cast<size_t>(m) * Np + n), -sh));
-#pragma unroll
-          for (int d = 0; d < 8; ++d)  // fixed trip count: out.p stays in the parameter space
-            if (d < out.count) out.p[d][static_cast<size_t>(m) * out.ldc + out.n_off + n] = v;
-        }
-      }
-    }
-    if (out.fence_sys) __threadfence_system();
   };
 
-  int seg_rb = -1, seg_n = 0;
+  // chunk i of this CTA: stage j = i / kSkStageChunks at ring slot s with phase parity ph,
+  // position c in the stage, row block rb, k index kc -- advanced by kSkGroups chunks per
+  // iteration without divisions (one division each to start)
+  int c = q % kSkStageChunks;
+  int s = (q / kSkStageChunks) % stages;
+  uint32_t ph = ((q / kSkStageChunks) / stages) & 1;
+  const long long uq = u0 + q;
+  int rb = static_cast<int>(uq / k_blocks);
+  int kc = static_cast<int>(uq - static_cast<long long>(rb) * k_blocks);
+  int seg_rb = -1;
   for (int i = q; i < n_my; i += kSkGroups) {
-    const long long u = u0 + i;
-    const int rb = static_cast<int>(u / k_blocks);
-    const int kc = static_cast<int>(u - static_cast<long long>(rb) * k_blocks);
     if (rb != seg_rb) {
-      if (seg_rb >= 0) flush(seg_rb, seg_n);
+      if (seg_rb >= 0) flush(seg_rb);
       seg_rb = rb;
-      seg_n = 0;
     }
-    const int s = i % stages;
-    if (!warp_wait(&full[s], (i / stages) & 1, kErrWaitFull, abort_flag)) {
+    if (!(MXFP4_SK_DIAG & 2) && !warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
       seg_rb = -1;  // aborted: this segment's sums stay incomplete (the error word says so)
       break;
     }
-    const uint32_t st = smem_u32(smem + s * sbytes);
-    uint4 dw[2];
-    uint32_t sw[2];
-#pragma unroll
-    for (int a = 0; a < 2; ++a) {
-      dw[a] = lds128(st + lane_d[a]);
-      sw[a] = lds32(st + lane_s[a]);
-    }
-    const uint32_t xs = st + kChunkBytes;
-#pragma unroll
-    for (int G = 0; G < 2; ++G) {
-      const uint32_t slot = static_cast<uint32_t>(t ^ ((2 * kc + G) & 3)) * 16;
-      uint4 xb[NT];
-#pragma unroll
-      for (int jt = 0; jt < NT; ++jt) {
-        xb[jt] = make_uint4(0, 0, 0, 0);
-        if (row_live[jt]) xb[jt] = lds128(xs + G * x_g1 + xrow[jt] + slot);
-      }
+    const uint32_t st = smem_u32(smem + s * sbytes) + c * kChunkBytes;  // this chunk's weights
+    const uint32_t xs = smem_u32(smem + s * sbytes) + kSkStageChunks * kChunkBytes + c * xbytes;  // activations
+    if (!(MXFP4_SK_DIAG & 1)) {
+      uint4 dw[2];
+      uint32_t sw[2];
 #pragma unroll
       for (int a = 0; a < 2; ++a) {
-        const uint32_t wl = G ? dw[a].z : dw[a].x;  // row g, group G
-        const uint32_t wh = G ? dw[a].w : dw[a].y;  // row g + 8, group G
-        // scale bytes (g,G0) (g+8,G0) (g,G1) (g+8,G1) -> 2**(s-127) as f32 bits (s << 23); a
-        // zero byte (2**-127) decodes to 0, a difference far below the error bound
-        const float sl = __uint_as_float((sw[a] << (23 - 16 * G)) & 0x7F800000u);
-        const float sh = __uint_as_float(G ? (sw[a] >> 1) & 0x7F800000u : (sw[a] << 15) & 0x7F800000u);
-        uint32_t fl[4], fh[4];
-        e2m1x8_to_f16x2(wl, fl);
-        e2m1x8_to_f16x2(wh, fh);
+        dw[a] = lds128(st + lane_d[a]);
+        sw[a] = lds32(st + lane_s[a]);
+      }
+#pragma unroll
+      for (int G = 0; G < 2; ++G) {
+        const uint32_t slot = static_cast<uint32_t>(t ^ ((2 * kc + G) & 3)) * 16;
+        uint4 xb[NT];
 #pragma unroll
         for (int jt = 0; jt < NT; ++jt) {
-          float dd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          mma_f16_16816(dd, fl[0], fh[0], fl[1], fh[1], xb[jt].x, xb[jt].y);
-          mma_f16_16816(dd, fl[2], fh[2], fl[3], fh[3], xb[jt].z, xb[jt].w);
-          accr[a][jt][0] = fmaf(dd[0], sl, accr[a][jt][0]);
-          accr[a][jt][1] = fmaf(dd[1], sl, accr[a][jt][1]);
-          accr[a][jt][2] = fmaf(dd[2], sh, accr[a][jt][2]);
-          accr[a][jt][3] = fmaf(dd[3], sh, accr[a][jt][3]);
+          xb[jt] = make_uint4(0, 0, 0, 0);
+          if (row_live[jt]) xb[jt] = lds128(xs + G * x_g1 + xrow[jt] + slot);
+        }
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          const uint32_t wl = G ? dw[a].z : dw[a].x;  // row g, group G
+          const uint32_t wh = G ? dw[a].w : dw[a].y;  // row g + 8, group G
+          // scale bytes (g,G0) (g+8,G0) (g,G1) (g+8,G1) -> 2**(s-127) as f32 bits (s << 23); a
+          // zero byte (2**-127) decodes to 0, a difference far below the error bound
+          const float sl = __uint_as_float((sw[a] << (23 - 16 * G)) & 0x7F800000u);
+          const float sh = __uint_as_float(G ? (sw[a] >> 1) & 0x7F800000u : (sw[a] << 15) & 0x7F800000u);
+          uint32_t fl[4], fh[4];
+          e2m1x8_to_f16x2(wl, fl);
+          e2m1x8_to_f16x2(wh, fh);
+#pragma unroll
+          for (int jt = 0; jt < NT; ++jt) {
+            float dd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            mma_f16_16816(dd, fl[0], fh[0], fl[1], fh[1], xb[jt].x, xb[jt].y);
+            mma_f16_16816(dd, fl[2], fh[2], fl[3], fh[3], xb[jt].z, xb[jt].w);
+            accr[a][jt][0] = fmaf(dd[0], sl, accr[a][jt][0]);
+            accr[a][jt][1] = fmaf(dd[1], sl, accr[a][jt][1]);
+            accr[a][jt][2] = fmaf(dd[2], sh, accr[a][jt][2]);
+            accr[a][jt][3] = fmaf(dd[3], sh, accr[a][jt][3]);
+          }
         }
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    ++seg_n;
+    c += kSkGroups;
+    while (c >= kSkStageChunks) {
+      c -= kSkStageChunks;
+      if (++s == stages) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
+    kc += kSkGroups;
+    while (kc >= k_blocks) {
+      kc -= k_blocks;
+      ++rb;
+    }
   }
-  if (seg_rb >= 0) flush(seg_rb, seg_n);
+  if (seg_rb >= 0) flush(seg_rb);
+}
+
+// fp32 sums [M][Np] -> C[m][n] = sums * 2**-shift[m] for n < N, to every destination.  Two
+// outputs per thread and grid-stride iteration.
+template <typename OutT>
+__global__ void __launch_bounds__(256) gemv_sk_finalize_kernel(const float* __restrict__ acc,
+                                                               const int* __restrict__ xshift, int M, int N, int Np,
+                                                               const GvOut<OutT> out) {
+  griddep_wait();  // the decode kernel's reductions are complete
+  const int half = (N + 1) / 2;
+  const long long total = static_cast<long long>(M) * half;
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * 256) {
+    const int m = static_cast<int>(i / half);
+    const int n = 2 * static_cast<int>(i - static_cast<long long>(m) * half);
+    const int sh = xshift[m];
+    const float2 v = *reinterpret_cast<const float2*>(acc + static_cast<size_t>(m) * Np + n);
+    const OutT a = gv_out<OutT>(ldexpf(v.x, -sh)), b = gv_out<OutT>(ldexpf(v.y, -sh));
+#pragma unroll
+    for (int d = 0; d < 8; ++d)  // fixed trip count: out.p stays in the parameter space
+      if (d < out.count) {
+        OutT* row = out.p[d] + static_cast<size_t>(m) * out.ldc + out.n_off;
+        row[n] = a;
+        if (n + 1 < N) row[n + 1] = b;
+      }
+  }
+  if (out.fence_sys) __threadfence_system();
 }
 
 }  // namespace mxb

@@ -309,22 +309,34 @@ int gemv_kernel_knob() {
 }
 bool gemv_use_tc() { return gemv_kernel_knob() == 2; }
 
-// Workspace of the stream-K decode path (0 when M is outside its range).
+// Workspace of the stream-K decode path (0 when the shape is outside its range: M <= 16, and
+// K <= 32768 so that one prestage thread holds its share of an activation row).
 size_t gemv_sk_bytes(int M, int N, int K) {
-  if (M < 1 || M > 16) return 0;
+  if (M < 1 || M > 16 || k_blocks_of(K) * 8 > kSkPreThreads * kSkPreVecs) return 0;
   return sk_workspace(M, n_blocks_of(N), k_blocks_of(K)).total;
 }
 
-template <int NT, typename OutT>
-int launch_gemv_sk_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K, const SkWorkspace& w,
-                     uint8_t* ws, cudaStream_t stream, DeviceState* d) {
-  const int slot = (NT == 1 ? 0 : 2) + (sizeof(OutT) == 4 ? 0 : 1);
-  if (!d->sk_attr[slot]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_sk_kernel<NT, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         sk_smem_bytes(1) > sk_smem_bytes(16) ? sk_smem_bytes(1) : sk_smem_bytes(16));
-    if (e != cudaSuccess) return ret(e);
-    d->sk_attr[slot] = true;
-  }
+// Launch with the programmatic-dependent-launch attribute (unless MXFP4_NO_PDL=1): the kernel
+// may start while the launch before it in the stream (our own producer of its inputs) runs,
+// and waits with griddepcontrol.wait before it reads what that launch writes.
+template <typename... KArgs, typename... Args>
+int launch_pdl_grid(void (*kernel)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return ret(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
+template <typename OutT>
+int launch_gemv_sk_finalize(const OutSpec& o, int M, int N, const SkWorkspace& w, uint8_t* ws, cudaStream_t stream,
+                            DeviceState* d) {
   GvOut<OutT> out;
   std::memset(&out, 0, sizeof(out));
   for (int i = 0; i < o.count; ++i) out.p[i] = static_cast<OutT*>(o.dst[i]);
@@ -332,43 +344,45 @@ int launch_gemv_sk_t(const uint8_t* wpack, const OutSpec& o, int M, int N, int K
   out.ldc = o.ldc;
   out.n_off = o.n_off;
   out.fence_sys = o.fence_sys;
-  const int nb = n_blocks_of(N), kb = k_blocks_of(K);
-  const long long units = static_cast<long long>(nb) * kb;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(std::min<long long>(d->sm_count, units)), 1, 1);
-  cfg.blockDim = dim3(kSkThreads, 1, 1);
-  cfg.dynamicSmemBytes = sk_smem_bytes(M);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // after our prestage kernel
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_sk_kernel<NT, OutT>, wpack, M, N, kb, nb,
-                                     static_cast<const uint8_t*>(ws + w.x_off),
-                                     reinterpret_cast<const int*>(ws + w.shift_off),
-                                     reinterpret_cast<float*>(ws + w.acc_off), reinterpret_cast<int*>(ws + w.cnt_off),
-                                     out);
-  return ret(e);
+  const long long work = static_cast<long long>(M) * ((N + 1) / 2);
+  const int blocks = static_cast<int>(std::min<long long>((work + 255) / 256, 4LL * d->sm_count));
+  return launch_pdl_grid(gemv_sk_finalize_kernel<OutT>, dim3(blocks), 256, 0, stream,
+                         reinterpret_cast<const float*>(ws + w.acc_off), reinterpret_cast<const int*>(ws + w.shift_off),
+                         M, N, n_blocks_of(N) * kChunkRows, out);
 }
 
-// Stream-K decode: prestage (activations to f16, sums and counters zeroed), then the kernel.
+// Stream-K decode: prestage (activations to f16, sums zeroed), the streaming kernel, then the
+// conversion of the sums to the output -- three launches chained by programmatic dependent launch.
 int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
                    uint8_t* ws, cudaStream_t stream, DeviceState* d) {
   const int nb = n_blocks_of(N), kb = k_blocks_of(K);
   const SkWorkspace w = sk_workspace(M, nb, kb);
   const long long zero_n4 = static_cast<long long>((w.total - w.acc_off) / 16);
-  const int grid = std::max(M, 2 * d->sm_count);
-  gemv_sk_prestage_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, kb, ws + w.x_off,
-                                                    reinterpret_cast<int*>(ws + w.shift_off),
-                                                    reinterpret_cast<float4*>(ws + w.acc_off), zero_n4);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return ret(e);
-  if (M <= 8)
-    return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_t<1, float>(wpack, C, M, N, K, w, ws, stream, d)
-                                      : launch_gemv_sk_t<1, __nv_bfloat16>(wpack, C, M, N, K, w, ws, stream, d);
-  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_t<2, float>(wpack, C, M, N, K, w, ws, stream, d)
-                                    : launch_gemv_sk_t<2, __nv_bfloat16>(wpack, C, M, N, K, w, ws, stream, d);
+  const int grid = std::max(M, d->sm_count);
+  gemv_sk_prestage_kernel<<<grid, kSkPreThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, kb,
+                                                             ws + w.x_off, reinterpret_cast<int*>(ws + w.shift_off),
+                                                             reinterpret_cast<float4*>(ws + w.acc_off), zero_n4);
+  int rc = launch_status();
+  if (rc) return rc;
+  const int slot = M <= 8 ? 0 : 1;
+  if (!d->sk_attr[slot]) {
+    cudaError_t e = M <= 8 ? cudaFuncSetAttribute(gemv_sk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  std::max(sk_smem_bytes(1), sk_smem_bytes(8)))
+                           : cudaFuncSetAttribute(gemv_sk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  std::max(sk_smem_bytes(9), sk_smem_bytes(16)));
+    if (e != cudaSuccess) return ret(e);
+    d->sk_attr[slot] = true;
+  }
+  const dim3 sk_grid(static_cast<unsigned>(std::min<long long>(d->sm_count, static_cast<long long>(nb) * kb)));
+  const uint8_t* xpre = ws + w.x_off;
+  float* acc = reinterpret_cast<float*>(ws + w.acc_off);
+  rc = M <= 8 ? launch_pdl_grid(gemv_sk_kernel<1>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
+                                xpre, acc)
+              : launch_pdl_grid(gemv_sk_kernel<2>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
+                                xpre, acc);
+  if (rc) return rc;
+  return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_finalize<float>(C, M, N, w, ws, stream, d)
+                                    : launch_gemv_sk_finalize<__nv_bfloat16>(C, M, N, w, ws, stream, d);
 }
 
 template <typename OutT>

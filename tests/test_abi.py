@@ -40,11 +40,21 @@ def test_abi_version_and_queries(L):
     assert lib.mxfp4_prepacked_bytes(3072, 3072) == 3072 * 3072 // 2 + 3072 * 3072 // 32
     assert lib.mxfp4_prepacked_bytes(200, 96) == 2 * 2 * 4352
     # prepacked weights need no workspace for large M (no GPU here, so no split-K plan); decode
-    # shapes (M <= 16) get optional room for the activations converted once per call: one 2 KiB
-    # f16 block (16 rows x 64 k) per 64-k chunk plus 256 bytes of row shifts
+    # shapes (M <= 16) get optional room for the stream-K decode kernel: the activations as f16
+    # (128*M bytes per 64-k chunk), 256 bytes of row shifts and fp32 sums [M][N rounded to 128],
+    # each part 256-byte aligned -- or at least the other decode kernels' prestaged activations
+    # (one 2 KiB block per chunk plus 256 bytes)
+    def al(x):
+        return -(-x // 256) * 256
+
+    def sk(M, N, K):
+        nb, kb = -(-N // 128), -(-K // 64)
+        return al(kb * 128 * M) + 256 + al(M * nb * 128 * 4)
+
     assert lib.mxfp4_gemm_workspace_bytes(32, 3072, 3072, L.LAYOUT_PREPACKED) == 0
-    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_PREPACKED) == 48 * 2048 + 256
-    assert lib.mxfp4_gemm_workspace_bytes(1, 3072, 3072, L.LAYOUT_PREPACKED) == 48 * 2048 + 256
+    assert lib.mxfp4_gemm_workspace_bytes(8, 3072, 3072, L.LAYOUT_PREPACKED) == max(sk(8, 3072, 3072), 48 * 2048 + 256)
+    assert lib.mxfp4_gemm_workspace_bytes(1, 3072, 3072, L.LAYOUT_PREPACKED) == max(sk(1, 3072, 3072), 48 * 2048 + 256)
+    assert lib.mxfp4_gemm_workspace_bytes(16, 57344, 8192, L.LAYOUT_PREPACKED) == sk(16, 57344, 8192)
     assert lib.mxfp4_gemm_workspace_bytes(32, 3072, 3072, L.LAYOUT_REF) == lib.mxfp4_prepacked_bytes(3072, 3072)
     assert lib.mxfp4_select_path(1, 8192, 8192) == L.PATH_GEMV
     assert lib.mxfp4_select_path(16, 8192, 8192) == L.PATH_GEMV

@@ -1,12 +1,12 @@
 """CPU model of the stream-K decode kernel's schedule (gemv_sk_kernel in csrc/gemm_small_sk.cuh).
 
 The kernel gives CTA c the chunk range [c*U/G, (c+1)*U/G) of the U = n_blocks * k_blocks
-(row block, k-chunk) units, row-block-major; group q of its four chunk groups takes the CTA's
-chunks i = q (mod 4); at every row-block change and at the end each of the group's four warps
-adds the number of chunks it covered to the row block's counter, and the warp whose addition
-reaches 4 * k_blocks writes the row block.  This model replays that bookkeeping: every unit is
-processed exactly once, every row block's count reaches exactly 4 * k_blocks, exactly one warp
-finalises each row block, and it does so only after every chunk of the row block was covered.
+(row block, k-chunk) units, row-block-major; group q of its five chunk groups takes the CTA's
+chunks i = q (mod 5); at every row-block change and at the end each of the group's four warps
+adds its partial sums of the row block (covering the chunks it processed) into the fp32 sums.
+This model replays that bookkeeping: every unit is processed exactly once, and the flushes of
+every row block together cover each of its k_blocks chunks with all four warps (32 rows each)
+exactly once, so the sums the finalize kernel converts are complete.
 """
 
 import itertools
@@ -20,9 +20,9 @@ def replay(n_blocks, k_blocks, grid):
     events = []  # (row block, chunks) flushes, in an arbitrary but complete order
     for c in range(grid):
         u0, u1 = U * c // grid, U * (c + 1) // grid
-        for q in range(4):
+        for q in range(5):
             seg_rb, seg_n = -1, 0
-            for i in range(q, u1 - u0, 4):
+            for i in range(q, u1 - u0, 5):
                 u = u0 + i
                 rb = u // k_blocks
                 if rb != seg_rb:
@@ -40,18 +40,14 @@ def replay(n_blocks, k_blocks, grid):
     (80, 128, 148), (64, 128, 148), (448, 128, 148), (64, 448, 148),  # decode shapes (N/128, K/64)
     (1, 1, 1), (1, 3, 1), (3, 5, 7), (2, 2, 148), (7, 13, 5), (5, 1, 3),
 ])
-def test_every_unit_once_and_one_finaliser_per_row_block(n_blocks, k_blocks, grid):
+def test_every_unit_once_and_every_row_block_fully_flushed(n_blocks, k_blocks, grid):
     grid = min(grid, n_blocks * k_blocks)
     seen, events = replay(n_blocks, k_blocks, grid)
     assert all(s == 1 for s in seen)
     count = [0] * n_blocks
-    finalisers = [0] * n_blocks
     for rb, n in events:
         count[rb] += n
-        if count[rb] == 4 * k_blocks:
-            finalisers[rb] += 1
     assert count == [4 * k_blocks] * n_blocks
-    assert finalisers == [1] * n_blocks
 
 
 def test_shares_differ_by_at_most_one_chunk():
