@@ -344,7 +344,11 @@ class Ctx:
         torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
         if self.world > 1:
-            dist.init_process_group("nccl", device_id=self.dev)
+            import datetime
+
+            # a rank that stops early makes the others fail within minutes instead of waiting in
+            # a collective for the default ten
+            dist.init_process_group("nccl", device_id=self.dev, timeout=datetime.timedelta(seconds=180))
 
     def barrier(self):
         if self.world > 1:

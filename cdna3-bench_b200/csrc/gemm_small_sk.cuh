@@ -9,20 +9,24 @@
 // * One CTA per SM, each streaming an equal, contiguous share of the (128-row weight block,
 //   64-k chunk) sequence in row-block-major order -- the shares differ by at most one chunk, so
 //   all SMs finish together whatever the shape.
-// * A producer warp keeps a ring of stages full, each stage kSkStageChunks consecutive chunks:
-//   one bulk copy of their weights (consecutive chunks are adjacent in memory, 17 KB) and one of
-//   their activation blocks (f16, 128*M bytes per chunk, pre-scaled per row by a power of two so
-//   that every bf16 value is exact, staged once per GEMM by gemv_sk_prestage_kernel).  The
-//   weights of the first ring-full of stages go out before the kernel waits for the prestage.
-// * 20 compute warps in 5 groups; group q takes the CTA's chunks i = q (mod 5) and each of its
-//   warps owns 32 weight rows (two m16 tiles) of the chunk.  Weights go through the hardware
-//   E2M1 -> f16 conversion (exact, unscaled) into mma.sync.m16n8k16 fragments with the
-//   activation rows as the n8 operand; each 32-element group's fp32 partial is multiplied by
-//   its E8M0 scale 2**(s-127) and accumulated in fp32 registers.  Ring positions and row-block
-//   and k indices advance incrementally: no integer division in the streaming loops.
+// * A producer warp keeps a ring of stages full, each stage kSkStageChunks consecutive chunks of
+//   weights fetched with one bulk copy (consecutive chunks of the row-block-major sequence are
+//   adjacent in memory: 17 KB per copy).  The activations do not travel through the copy engine
+//   (a small copy costs it as much time as a large one): they are staged once per GEMM by
+//   gemv_sk_prestage_kernel (f16, pre-scaled per row by a power of two so that every bf16 value
+//   is exact; 128*M bytes per chunk, L2-resident) and each compute warp loads its fragments of
+//   the next chunk it will process with plain 16-byte loads while it computes the current one.
+// * 16 compute warps in groups of WPC (1 for M <= 8, 2 above); group q takes the CTA's chunks
+//   i = q (mod 16/WPC) and each of its warps owns 128/WPC weight rows (8/WPC m16 tiles) of the
+//   chunk, so the per-chunk work of waiting, indexing and loading activations is paid once per
+//   128 or 64 rows.  Weights go through the hardware E2M1 -> f16 conversion (exact, unscaled)
+//   into mma.sync.m16n8k16 fragments with the activation rows as the n8 operand; each
+//   32-element group's fp32 partial is multiplied by its E8M0 scale 2**(s-127) and accumulated
+//   in fp32 registers.  Ring positions and row-block and k indices advance incrementally: no
+//   integer division in the streaming loops.
 // * At the end of each row-block segment every warp adds its partial sums into an fp32 buffer
-//   in workspace (zeroed by the prestage kernel) with global reductions: several CTAs (and the
-//   five groups of one CTA) hold parts of a row block.  No warp waits for another one: there is
+//   in workspace (zeroed by the prestage kernel) with global reductions: several CTAs (and
+//   several groups of one CTA) hold parts of a row block.  No warp waits for another one: there is
 //   no inter-CTA barrier and no named barrier, so a wait that gives up strands nobody.
 // * gemv_sk_finalize_kernel turns the sums into the output (undoing the activation row shifts),
 //   for every destination.
@@ -41,18 +45,18 @@ namespace mxb {
                          // reductions; results are wrong in these builds
 #endif
 
-constexpr int kSkGroups = 5;                     // chunk groups (chunks i = q mod 5)
-constexpr int kSkComputeWarps = 4 * kSkGroups;   // each group: 4 warps x 32 weight rows
-constexpr int kSkThreads = 32 * (kSkComputeWarps + 1);  // + 1 producer warp = 672
+constexpr int kSkComputeWarps = 16;  // consumers; a chunk is shared by WPC of them (template)
+constexpr int kSkThreads = 32 * (kSkComputeWarps + 1);  // + 1 producer warp = 544
 #ifndef MXFP4_SK_STAGE_CHUNKS
 #define MXFP4_SK_STAGE_CHUNKS 4
 #endif
 constexpr int kSkStageChunks = MXFP4_SK_STAGE_CHUNKS;  // consecutive chunks per ring stage
 constexpr int kSkMaxStages = 64;
-constexpr int kSkRingBytes = 200 * 1024;
+constexpr int kSkRingBytes = 12 * kSkStageChunks * kChunkBytes;  // 204 KiB: twelve 4-chunk stages
 
-// Host and device agree on the ring from these.
-__host__ __device__ constexpr int sk_stage_bytes(int M) { return kSkStageChunks * (kChunkBytes + 128 * M); }
+// Host and device agree on the ring from these (the argument M is kept for the interface: the
+// ring holds weights only).
+__host__ __device__ constexpr int sk_stage_bytes(int M) { return (void)M, kSkStageChunks * kChunkBytes; }
 __host__ __device__ constexpr int sk_stages(int M) {
   return kSkRingBytes / sk_stage_bytes(M) < kSkMaxStages ? kSkRingBytes / sk_stage_bytes(M) : kSkMaxStages;
 }
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(kSkPreThreads) gemv_sk_prestage_kernel(const _
   }
 }
 
-template <int NT>
+template <int NT, int WPC>
 __global__ void __launch_bounds__(kSkThreads, 1)
     gemv_sk_kernel(const uint8_t* __restrict__ wpack, int M, int k_blocks, int n_blocks,
                    const uint8_t* __restrict__ xpre, float* __restrict__ acc) {
@@ -166,12 +170,12 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   const long long u0 = units * blockIdx.x / gridDim.x;
   const int n_my = static_cast<int>(units * (blockIdx.x + 1) / gridDim.x - u0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t xbytes = 128u * M;
+  const size_t xbytes = 128u * M;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 4 * kSkStageChunks);  // each chunk's four warps
+      mbar_init(&empty[i], WPC * kSkStageChunks);  // each chunk's WPC warps
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -185,43 +189,20 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       uint64_t pend = 0, pend_ph = 0;
       bool aborted = false;
       const int n_issue = (test_withhold() || (MXFP4_SK_DIAG & 2)) ? 0 : n_my;  // test switch: issue nothing
-      // Stage, its phase parity and the next activation block's k index advance without
-      // divisions.  The weights of the first `stages` stages go out before the wait for the
-      // prestage launch (they do not depend on it); their activation blocks follow it.
+      // stage and its phase parity advance without divisions; the weights do not depend on the
+      // prestage launch, so the producer never waits for it
       const int nst = (n_issue + kSkStageChunks - 1) / kSkStageChunks;
-      const int first = min(stages, nst);
-      int kc = static_cast<int>(u0 % k_blocks);
       const uint8_t* wsrc = wpack + u0 * kChunkBytes;
-      auto issue_x = [&](int j, int nch) {  // the stage's activation blocks, one copy per k run
-        uint8_t* xdst = smem + j * sbytes + kSkStageChunks * kChunkBytes;
-        for (int c = 0; c < nch;) {
-          const int run = min(nch - c, k_blocks - kc);
-          bulk_load(xdst + c * xbytes, xpre + static_cast<size_t>(kc) * xbytes, run * xbytes, &full[j]);
-          c += run;
-          kc += run;
-          if (kc == k_blocks) kc = 0;
-        }
-      };
-      for (int j = 0; j < first; ++j) {
-        const int nch = min(kSkStageChunks, n_issue - j * kSkStageChunks);
-        mbar_arrive_expect_tx(&full[j], nch * (kChunkBytes + xbytes));
-        bulk_load(smem + j * sbytes, wsrc, nch * kChunkBytes, &full[j]);
-        wsrc += nch * kChunkBytes;
-        pend |= 1ull << j;
-      }
-      if (first > 0) griddep_wait();  // the activations come from the prestage launch before this one
-      for (int j = 0; j < first; ++j) issue_x(j, min(kSkStageChunks, n_issue - j * kSkStageChunks));
-      int s = first == stages ? 0 : first;
-      uint32_t ph = first == stages ? 1 : 0;
-      for (int j = first; j < nst; ++j) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int j = 0; j < nst; ++j) {
         if (!mbar_wait(&empty[s], ph ^ 1, kErrWaitEmpty, abort_flag)) {
           aborted = true;
           break;
         }
         const int nch = min(kSkStageChunks, n_issue - j * kSkStageChunks);
-        mbar_arrive_expect_tx(&full[s], nch * (kChunkBytes + xbytes));
+        mbar_arrive_expect_tx(&full[s], nch * kChunkBytes);
         bulk_load(smem + s * sbytes, wsrc, nch * kChunkBytes, &full[s]);
-        issue_x(s, nch);
         pend |= 1ull << s;
         pend_ph = (pend_ph & ~(1ull << s)) | (static_cast<uint64_t>(ph) << s);
         wsrc += nch * kChunkBytes;
@@ -238,17 +219,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   }
 
   // -------------------------------------------------------------- compute warps
-  griddep_wait();  // the sums are zeroed
-  const int q = warp >> 2;   // chunk group
-  const int wq = warp & 3;   // rows 32*wq .. 32*wq+31 of every chunk
+  constexpr int NG = kSkComputeWarps / WPC;  // chunk groups
+  constexpr int RW = kChunkRows / WPC;       // weight rows per warp
+  constexpr int MT = RW / 16;                // m16 tiles per warp
+  static_assert(kSkComputeWarps % WPC == 0 && NG % kSkStageChunks == 0, "group layout");
+  griddep_wait();  // the sums are zeroed and the activations staged
+  const int q = warp / WPC;   // chunk group
+  const int wq = warp % WPC;  // rows RW*wq .. RW*wq+RW-1 of every chunk
   const int g = lane >> 2, t = lane & 3;
   const int Np = n_blocks * kChunkRows;
-  uint32_t lane_d[2], lane_s[2];
-#pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    lane_d[a] = chunk_unit(32 * wq + 16 * a + g, t) * 16;
-    lane_s[a] = kChunkData + (8 * (2 * wq + a) + g) * 4;
-  }
   bool row_live[NT];
   uint32_t xrow[NT];  // this lane's activation block offset for group G = 0 (without the slot)
 #pragma unroll
@@ -257,19 +236,32 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     xrow[jt] = (8 * jt + g) * 64;
   }
   const uint32_t x_g1 = static_cast<uint32_t>(M) * 64;  // group G = 1 starts M rows further
-  float accr[2][NT][4];
+  // this lane's activation fragments of the chunk with k index kx: block (G, row 8jt+g, slot)
+  auto load_x = [&](int kx, uint4 (&xb)[2][NT]) {
+    const uint8_t* base = xpre + static_cast<size_t>(kx) * xbytes;
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+    for (int G = 0; G < 2; ++G) {
+      const uint32_t slot = static_cast<uint32_t>(t ^ ((2 * kx + G) & 3)) * 16;
+#pragma unroll
+      for (int jt = 0; jt < NT; ++jt) {
+        xb[G][jt] = make_uint4(0, 0, 0, 0);
+        if (row_live[jt]) xb[G][jt] = __ldg(reinterpret_cast<const uint4*>(base + G * x_g1 + xrow[jt] + slot));
+      }
+    }
+  };
+  float accr[MT][NT][4];
+#pragma unroll
+  for (int a = 0; a < MT; ++a)
 #pragma unroll
     for (int j = 0; j < NT; ++j) accr[a][j][0] = accr[a][j][1] = accr[a][j][2] = accr[a][j][3] = 0.0f;
 
   // Adds this warp's partial sums of row block rb into the fp32 sums and clears them.
   auto flush = [&](int rb) {
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
+    for (int a = 0; a < MT; ++a)
 #pragma unroll
       for (int jt = 0; jt < NT; ++jt) {
-        const int n = rb * kChunkRows + 32 * wq + 16 * a + g;
+        const int n = rb * kChunkRows + RW * wq + 16 * a + g;
         const int m = 8 * jt + 2 * t;
         if ((MXFP4_SK_DIAG & 8) == 0 && m < M) {
           red_add_f32(acc + static_cast<size_t>(m) * Np + n, accr[a][jt][0]);
@@ -283,17 +275,28 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       }
   };
 
-  // chunk i of this CTA: stage j = i / kSkStageChunks at ring slot s with phase parity ph,
-  // position c in the stage, row block rb, k index kc -- advanced by kSkGroups chunks per
-  // iteration without divisions (one division each to start)
-  int c = q % kSkStageChunks;
+  // chunk i of this CTA: stage i / kSkStageChunks at ring slot s with phase parity ph, position
+  // c in the stage, row block rb, k index kc -- advanced by NG chunks per iteration (NG is a
+  // multiple of the stage size, so c stays and the slot moves by NG / kSkStageChunks)
+  const int c = q % kSkStageChunks;
   int s = (q / kSkStageChunks) % stages;
   uint32_t ph = ((q / kSkStageChunks) / stages) & 1;
   const long long uq = u0 + q;
   int rb = static_cast<int>(uq / k_blocks);
   int kc = static_cast<int>(uq - static_cast<long long>(rb) * k_blocks);
   int seg_rb = -1;
-  for (int i = q; i < n_my; i += kSkGroups) {
+  uint4 xcur[2][NT], xnext[2][NT];
+  if (q < n_my) load_x(kc, xcur);
+  // m16 tile a of this warp: rows 16 (MT wq + a) + g and + 8; its unit lies 32 units (512 bytes)
+  // further per tile and its scale word 8 words further (chunk_unit / chunk_scale_off)
+  const uint32_t lane_u = static_cast<uint32_t>(chunk_unit(RW * wq + g, t)) * 16;
+  const uint32_t lane_s = kChunkData + (8 * (MT * wq) + g) * 4;
+  for (int i = q; i < n_my; i += NG) {
+    {  // prefetch the activations of this group's next chunk
+      int kn = kc + NG;
+      while (kn >= k_blocks) kn -= k_blocks;
+      if (i + NG < n_my) load_x(kn, xnext);
+    }
     if (rb != seg_rb) {
       if (seg_rb >= 0) flush(seg_rb);
       seg_rb = rb;
@@ -303,40 +306,27 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       break;
     }
     const uint32_t st = smem_u32(smem + s * sbytes) + c * kChunkBytes;  // this chunk's weights
-    const uint32_t xs = smem_u32(smem + s * sbytes) + kSkStageChunks * kChunkBytes + c * xbytes;  // activations
     if (!(MXFP4_SK_DIAG & 1)) {
-      uint4 dw[2];
-      uint32_t sw[2];
 #pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        dw[a] = lds128(st + lane_d[a]);
-        sw[a] = lds32(st + lane_s[a]);
-      }
+      for (int a = 0; a < MT; ++a) {
+        const uint4 dw = lds128(st + lane_u + a * 512);
+        const uint32_t sw = lds32(st + lane_s + a * 32);
 #pragma unroll
-      for (int G = 0; G < 2; ++G) {
-        const uint32_t slot = static_cast<uint32_t>(t ^ ((2 * kc + G) & 3)) * 16;
-        uint4 xb[NT];
-#pragma unroll
-        for (int jt = 0; jt < NT; ++jt) {
-          xb[jt] = make_uint4(0, 0, 0, 0);
-          if (row_live[jt]) xb[jt] = lds128(xs + G * x_g1 + xrow[jt] + slot);
-        }
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          const uint32_t wl = G ? dw[a].z : dw[a].x;  // row g, group G
-          const uint32_t wh = G ? dw[a].w : dw[a].y;  // row g + 8, group G
+        for (int G = 0; G < 2; ++G) {
+          const uint32_t wl = G ? dw.z : dw.x;  // row g, group G
+          const uint32_t wh = G ? dw.w : dw.y;  // row g + 8, group G
           // scale bytes (g,G0) (g+8,G0) (g,G1) (g+8,G1) -> 2**(s-127) as f32 bits (s << 23); a
           // zero byte (2**-127) decodes to 0, a difference far below the error bound
-          const float sl = __uint_as_float((sw[a] << (23 - 16 * G)) & 0x7F800000u);
-          const float sh = __uint_as_float(G ? (sw[a] >> 1) & 0x7F800000u : (sw[a] << 15) & 0x7F800000u);
+          const float sl = __uint_as_float((sw << (23 - 16 * G)) & 0x7F800000u);
+          const float sh = __uint_as_float(G ? (sw >> 1) & 0x7F800000u : (sw << 15) & 0x7F800000u);
           uint32_t fl[4], fh[4];
           e2m1x8_to_f16x2(wl, fl);
           e2m1x8_to_f16x2(wh, fh);
 #pragma unroll
           for (int jt = 0; jt < NT; ++jt) {
             float dd[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            mma_f16_16816(dd, fl[0], fh[0], fl[1], fh[1], xb[jt].x, xb[jt].y);
-            mma_f16_16816(dd, fl[2], fh[2], fl[3], fh[3], xb[jt].z, xb[jt].w);
+            mma_f16_16816(dd, fl[0], fh[0], fl[1], fh[1], xcur[G][jt].x, xcur[G][jt].y);
+            mma_f16_16816(dd, fl[2], fh[2], fl[3], fh[3], xcur[G][jt].z, xcur[G][jt].w);
             accr[a][jt][0] = fmaf(dd[0], sl, accr[a][jt][0]);
             accr[a][jt][1] = fmaf(dd[1], sl, accr[a][jt][1]);
             accr[a][jt][2] = fmaf(dd[2], sh, accr[a][jt][2]);
@@ -347,19 +337,20 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    c += kSkGroups;
-    while (c >= kSkStageChunks) {
-      c -= kSkStageChunks;
-      if (++s == stages) {
-        s = 0;
-        ph ^= 1;
-      }
+    s += NG / kSkStageChunks;
+    if (s >= stages) {
+      s -= stages;
+      ph ^= 1;
     }
-    kc += kSkGroups;
+    kc += NG;
     while (kc >= k_blocks) {
       kc -= k_blocks;
       ++rb;
     }
+#pragma unroll
+    for (int G = 0; G < 2; ++G)
+#pragma unroll
+      for (int jt = 0; jt < NT; ++jt) xcur[G][jt] = xnext[G][jt];
   }
   if (seg_rb >= 0) flush(seg_rb);
 }

@@ -351,6 +351,12 @@ int launch_gemv_sk_finalize(const OutSpec& o, int M, int N, const SkWorkspace& w
                          M, N, n_blocks_of(N) * kChunkRows, out);
 }
 
+// Warps per chunk of the stream-K decode kernel for 8 < M <= 16 (two n8 activation tiles).
+#ifndef MXFP4_SK_WPC_WIDE
+#define MXFP4_SK_WPC_WIDE 4
+#endif
+constexpr int kSkWpcWide = MXFP4_SK_WPC_WIDE;
+
 // Stream-K decode: prestage (activations to f16, sums zeroed), the streaming kernel, then the
 // conversion of the sums to the output -- three launches chained by programmatic dependent launch.
 int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_dtype, int M, int N, int K,
@@ -366,9 +372,9 @@ int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_
   if (rc) return rc;
   const int slot = M <= 8 ? 0 : 1;
   if (!d->sk_attr[slot]) {
-    cudaError_t e = M <= 8 ? cudaFuncSetAttribute(gemv_sk_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = M <= 8 ? cudaFuncSetAttribute(gemv_sk_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   std::max(sk_smem_bytes(1), sk_smem_bytes(8)))
-                           : cudaFuncSetAttribute(gemv_sk_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           : cudaFuncSetAttribute(gemv_sk_kernel<2, kSkWpcWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   std::max(sk_smem_bytes(9), sk_smem_bytes(16)));
     if (e != cudaSuccess) return ret(e);
     d->sk_attr[slot] = true;
@@ -376,9 +382,9 @@ int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_
   const dim3 sk_grid(static_cast<unsigned>(std::min<long long>(d->sm_count, static_cast<long long>(nb) * kb)));
   const uint8_t* xpre = ws + w.x_off;
   float* acc = reinterpret_cast<float*>(ws + w.acc_off);
-  rc = M <= 8 ? launch_pdl_grid(gemv_sk_kernel<1>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
+  rc = M <= 8 ? launch_pdl_grid(gemv_sk_kernel<1, 1>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
                                 xpre, acc)
-              : launch_pdl_grid(gemv_sk_kernel<2>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
+              : launch_pdl_grid(gemv_sk_kernel<2, kSkWpcWide>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
                                 xpre, acc);
   if (rc) return rc;
   return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_finalize<float>(C, M, N, w, ws, stream, d)
