@@ -7,7 +7,7 @@ every row-block change and at the end each of the group's WPC warps adds its par
 row block (covering the chunks it processed) into the fp32 sums.  This model replays that
 bookkeeping: every unit is processed exactly once, and the flushes of every row block together
 cover each of its k_blocks chunks with all WPC warps (128 / WPC rows each) exactly once, so the
-sums the finalize kernel converts are complete.
+sums the finalize kernel converts are complete (gemv_sk_finalize_kernel).
 """
 
 import itertools
