@@ -42,7 +42,8 @@ namespace mxb {
 #ifndef MXFP4_SK_DIAG
 #define MXFP4_SK_DIAG 0  // sweep-only: 1 = consumers skip the arithmetic, 2 = the producer issues nothing
                          // and the consumers do not wait for it (compute rate alone), 8 = no global
-                         // reductions; results are wrong in these builds
+                         // reductions, 16 = no finalize launch, 32 = no prestage launch; results are
+                         // wrong in these builds
 #endif
 
 constexpr int kSkComputeWarps = 16;  // consumers; a chunk is shared by WPC of them (template)

@@ -356,6 +356,11 @@ int launch_gemv_sk_finalize(const OutSpec& o, int M, int N, const SkWorkspace& w
 #define MXFP4_SK_WPC_WIDE 4
 #endif
 constexpr int kSkWpcWide = MXFP4_SK_WPC_WIDE;
+// ... and for M <= 8 (one n8 activation tile).
+#ifndef MXFP4_SK_WPC_NARROW
+#define MXFP4_SK_WPC_NARROW 1
+#endif
+constexpr int kSkWpcNarrow = MXFP4_SK_WPC_NARROW;
 
 // Stream-K decode: prestage (activations to f16, sums zeroed), the streaming kernel, then the
 // conversion of the sums to the output -- three launches chained by programmatic dependent launch.
@@ -365,6 +370,7 @@ int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_
   const SkWorkspace w = sk_workspace(M, nb, kb);
   const long long zero_n4 = static_cast<long long>((w.total - w.acc_off) / 16);
   const int grid = std::max(M, d->sm_count);
+  if (!(MXFP4_SK_DIAG & 32))
   gemv_sk_prestage_kernel<<<grid, kSkPreThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(A), M, K, kb,
                                                              ws + w.x_off, reinterpret_cast<int*>(ws + w.shift_off),
                                                              reinterpret_cast<float4*>(ws + w.acc_off), zero_n4);
@@ -372,7 +378,7 @@ int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_
   if (rc) return rc;
   const int slot = M <= 8 ? 0 : 1;
   if (!d->sk_attr[slot]) {
-    cudaError_t e = M <= 8 ? cudaFuncSetAttribute(gemv_sk_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = M <= 8 ? cudaFuncSetAttribute(gemv_sk_kernel<1, kSkWpcNarrow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   std::max(sk_smem_bytes(1), sk_smem_bytes(8)))
                            : cudaFuncSetAttribute(gemv_sk_kernel<2, kSkWpcWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   std::max(sk_smem_bytes(9), sk_smem_bytes(16)));
@@ -382,11 +388,12 @@ int launch_gemv_sk(const void* A, const uint8_t* wpack, const OutSpec& C, int c_
   const dim3 sk_grid(static_cast<unsigned>(std::min<long long>(d->sm_count, static_cast<long long>(nb) * kb)));
   const uint8_t* xpre = ws + w.x_off;
   float* acc = reinterpret_cast<float*>(ws + w.acc_off);
-  rc = M <= 8 ? launch_pdl_grid(gemv_sk_kernel<1, 1>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
+  rc = M <= 8 ? launch_pdl_grid(gemv_sk_kernel<1, kSkWpcNarrow>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
                                 xpre, acc)
               : launch_pdl_grid(gemv_sk_kernel<2, kSkWpcWide>, sk_grid, kSkThreads, sk_smem_bytes(M), stream, wpack, M, kb, nb,
                                 xpre, acc);
   if (rc) return rc;
+  if (MXFP4_SK_DIAG & 16) return 0;
   return c_dtype == MXFP4_DTYPE_F32 ? launch_gemv_sk_finalize<float>(C, M, N, w, ws, stream, d)
                                     : launch_gemv_sk_finalize<__nv_bfloat16>(C, M, N, w, ws, stream, d);
 }
