@@ -24,10 +24,12 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
   the same box -- the chained FLUX block (flux_chain) and the decode shapes at M = 1, 4, 16 --
   each timed the same way with its own roofline fraction.
 * N > 1 (torchrun, NCCL): strong scaling of the same block, column-parallel: every GEMM's N is
-  split over the ranks in whole 128-row tiles and the all-gather is fused into the GEMM
-  epilogue (each output tile is stored into every GPU's full [M, N] output over NVLink), so
-  every GPU ends the step holding the whole block's outputs.  `--unfused` gives the baseline
-  (local GEMM, then an NCCL all-gather).  tp_sweep is BASELINE configs[4] in the same form.
+  split over the ranks in whole 128-row tiles and an NCCL all-gather after each GEMM gives every
+  GPU the whole block's outputs.  `--fused` fuses the all-gather into the GEMM epilogue instead
+  (each output tile stored into every GPU's full [M, N] output over NVLink): about twice as fast
+  at 2 and 4 GPUs, but with many destinations an occasional call stalls until the kernels'
+  bounded waits give up, so it is not the default.  tp_sweep is BASELINE configs[4] in the same
+  form.
 """
 
 from __future__ import annotations
@@ -87,8 +89,10 @@ def parse(argv=None):
     ap.add_argument("--weak", action="store_true",
                     help="N > 1: each rank its own N-slice of a w-times wider layer, no collective (weak scaling)")
     ap.add_argument("--unfused", action="store_true",
-                    help="N > 1: GEMM then a separate NCCL all-gather (default: all-gather fused into the GEMM "
-                         "epilogue, stores straight into every GPU's output over NVLink)")
+                    help="N > 1: GEMM then a separate NCCL all-gather (the default)")
+    ap.add_argument("--fused", action="store_true",
+                    help="N > 1: the all-gather fused into the GEMM epilogue, stores straight into every GPU's "
+                         "output over NVLink (faster; with many destinations it stalls on rare calls, see DESIGN)")
     ap.add_argument("--no-graph", action="store_true",
                     help="decode and c0 workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
     return ap.parse_args(argv)
@@ -370,7 +374,7 @@ def tp_mode(args, ctx, workload: str) -> str:
         return "single"
     if args.weak and workload != "tp_sweep":
         return "weak"
-    return "unfused" if args.unfused else "fused"
+    return "fused" if args.fused and not args.unfused else "unfused"
 
 
 def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -> dict:
