@@ -24,8 +24,8 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
   the same box -- the chained FLUX block (flux_chain) and the decode shapes at M = 1, 4, 16 --
   each timed the same way with its own roofline fraction.
 * N > 1 (torchrun, NCCL): strong scaling of the same block, column-parallel: every GEMM's N is
-  split over the ranks in whole 128-row tiles and an NCCL all-gather after each GEMM gives every
-  GPU the whole block's outputs.  `--fused` fuses the all-gather into the GEMM epilogue instead
+  split over the ranks in whole 128-row tiles and an NCCL all-gather after each GEMM (on a second
+  stream, overlapping the next GEMM) gives every GPU the whole block's outputs.  `--fused` fuses the all-gather into the GEMM epilogue instead
   (each output tile stored into every GPU's full [M, N] output over NVLink): about twice as fast
   at 2 and 4 GPUs, but with many destinations an occasional call stalls until the kernels'
   bounded waits give up, so it is not the default.  tp_sweep is BASELINE configs[4] in the same
@@ -445,6 +445,8 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
         return mx.gemm(it["A"], w, C=it["C"])
 
     peer = None
+    comm = torch.cuda.Stream(dev) if mode == "unfused" else None
+    gathered = [None] * len(items)
     if mode == "fused":
         peer = [sharding.PeerOutput(M, it["N_full"], torch.bfloat16) for it in items]
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
@@ -462,9 +464,17 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
             if record:
                 ev[i_step][j][1].record()
             if mode == "unfused":
-                sharding.all_gather_columns(it["C"], it["N_full"])
+                # the all-gather of this GEMM's slice runs on its own stream while the next GEMM
+                # computes (the block's four GEMMs are independent)
+                done = torch.cuda.Event()
+                done.record()
+                comm.wait_event(done)
+                with torch.cuda.stream(comm):
+                    gathered[j] = sharding.all_gather_columns(it["C"], it["N_full"])
         if mode == "fused":  # one stream-ordered collective: every peer's stores have landed
             peer[-1].sync()
+        if mode == "unfused":  # the step ends when every gather has landed
+            torch.cuda.current_stream().wait_stream(comm)
 
     for i in range(warmup):
         step(i, False)
@@ -612,7 +622,8 @@ def parallelism_text(mode: str, world: int) -> str:
             "weak": f"weak x{world}: each rank its own N-slice of a {world}x wider layer, no collective",
             "fused": f"tp{world} column-parallel, all-gather fused into the GEMM epilogue (NVLink stores into every "
                      "GPU's full output)",
-            "unfused": f"tp{world} column-parallel, local GEMM + NCCL all-gather"}[mode]
+            "unfused": f"tp{world} column-parallel, local GEMM + NCCL all-gather (each gather overlapped with "
+                       "the next GEMM on a second stream)"}[mode]
 
 
 def main():
