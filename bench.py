@@ -23,13 +23,14 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
 * extra (N = 1, default workload only): the other measured workloads of the same library on
   the same box -- the chained FLUX block (flux_chain) and the decode shapes at M = 1, 4, 16 --
   each timed the same way with its own roofline fraction.
-* N > 1 (torchrun, NCCL): strong scaling of the same block, column-parallel: every GEMM's N is
-  split over the ranks in whole 128-row tiles and an NCCL all-gather after each GEMM (on a second
-  stream, overlapping the next GEMM) gives every GPU the whole block's outputs.  `--fused` fuses the all-gather into the GEMM epilogue instead
-  (each output tile stored into every GPU's full [M, N] output over NVLink): about twice as fast
-  at 2 and 4 GPUs, but with many destinations an occasional call stalls until the kernels'
-  bounded waits give up, so it is not the default.  tp_sweep is BASELINE configs[4] in the same
-  form.
+* N > 1 (torchrun): strong scaling of the same block, column-parallel: every GEMM's N is
+  split over the ranks in whole 128-row tiles; each GEMM writes its slice into this GPU's full
+  [M, N] output and the copy engines push the slice into every peer's output over NVLink (one
+  pitched copy per peer, CUDA IPC buffers) while the next GEMM computes; one stream-ordered
+  one-int NCCL all-reduce per step orders the reads.  `--fused` stores every tile into all GPUs'
+  outputs from the GEMM epilogue instead (with many destinations an occasional call stalls until
+  the kernels' bounded waits give up, so it is opt-in); `--unfused` uses an NCCL all-gather per
+  GEMM.  tp_sweep is BASELINE configs[4] in the same form.
 """
 
 from __future__ import annotations
@@ -69,6 +70,7 @@ METRICS = {
     "decode_m16": ("decode_m16_hbm_gbs", "GB/s"),
     "tp_sweep": ("tp_sweep_tflops", "TFLOP/s"),
 }
+TP_MODES = ("fused", "unfused", "ce")  # column-parallel modes (strong scaling)
 NVLINK_GBS = 770.0  # measured peer copy per direction on this pool's B200s
 EXTRA_WORKLOADS = ("flux_chain", "decode_m1", "decode_m4", "decode_m16")
 
@@ -89,10 +91,13 @@ def parse(argv=None):
     ap.add_argument("--weak", action="store_true",
                     help="N > 1: each rank its own N-slice of a w-times wider layer, no collective (weak scaling)")
     ap.add_argument("--unfused", action="store_true",
-                    help="N > 1: GEMM then a separate NCCL all-gather (the default)")
+                    help="N > 1: GEMM then a separate NCCL all-gather on a second stream")
     ap.add_argument("--fused", action="store_true",
                     help="N > 1: the all-gather fused into the GEMM epilogue, stores straight into every GPU's "
                          "output over NVLink (faster; with many destinations it stalls on rare calls, see DESIGN)")
+    ap.add_argument("--ce", action="store_true",
+                    help="N > 1 (the default): each GEMM writes its slice into this GPU's full output and the "
+                         "copy engines push it to every peer over NVLink while the next GEMM computes")
     ap.add_argument("--no-graph", action="store_true",
                     help="decode and c0 workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
     return ap.parse_args(argv)
@@ -374,7 +379,9 @@ def tp_mode(args, ctx, workload: str) -> str:
         return "single"
     if args.weak and workload != "tp_sweep":
         return "weak"
-    return "fused" if args.fused and not args.unfused else "unfused"
+    if args.unfused:
+        return "unfused"
+    return "fused" if args.fused else "ce"
 
 
 def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -> dict:
@@ -399,7 +406,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
     # computes its own slice of a w-times wider layer, i.e. the full per-rank shape)
     gemms = []
     for name, N, K in full:
-        if mode in ("fused", "unfused"):
+        if mode in TP_MODES:
             n0, n1 = sharding.column_slice(N, world, rank)
             gemms.append((name, N, n0, n1 - n0, K))
         else:
@@ -419,7 +426,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
     # rank's own work, summed over ranks)
     flops_rank = sum(2.0 * M * it["N"] * it["K"] for it in items)
     bytes_rank = sum(cost_model.Shape(M, it["N"], it["K"]).in_bytes for it in items)
-    if mode in ("fused", "unfused"):
+    if mode in TP_MODES:
         units_job = sum(cost_model.Shape(M, N, K).in_bytes if decode else 2.0 * M * N * K for _, N, K in full)
     else:
         units_job = world * (bytes_rank if decode else flops_rank)
@@ -447,8 +454,9 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
     peer = None
     comm = torch.cuda.Stream(dev) if mode == "unfused" else None
     gathered = [None] * len(items)
-    if mode == "fused":
+    if mode in ("fused", "ce"):
         peer = [sharding.PeerOutput(M, it["N_full"], torch.bfloat16) for it in items]
+    ce_streams = [torch.cuda.Stream(dev) for _ in range(world - 1)] if mode == "ce" else None
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in items]
           for _ in range(steps)]
 
@@ -459,6 +467,8 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
                 ev[i_step][j][0].record()
             if mode == "fused":
                 kk.gemm_allgather(it["A"], w, peer[j].ptrs, it["n0"], it["N_full"])
+            elif mode == "ce":
+                kk.gemm_allgather(it["A"], w, [peer[j].ptrs[rank]], it["n0"], it["N_full"])
             else:
                 run_gemm(it, w)
             if record:
@@ -471,7 +481,18 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
                 comm.wait_event(done)
                 with torch.cuda.stream(comm):
                     gathered[j] = sharding.all_gather_columns(it["C"], it["N_full"])
-        if mode == "fused":  # one stream-ordered collective: every peer's stores have landed
+            if mode == "ce":
+                # the copy engines push this slice to every peer (one stream per peer) while the
+                # next GEMM computes
+                done = torch.cuda.Event()
+                done.record()
+                for cs in ce_streams:
+                    cs.wait_event(done)
+                peer[j].push(it["n0"], it["n0"] + it["N"], ce_streams)
+        if mode == "ce":
+            for cs in ce_streams:
+                torch.cuda.current_stream().wait_stream(cs)
+        if mode in ("fused", "ce"):  # one stream-ordered collective: every peer's stores have landed
             peer[-1].sync()
         if mode == "unfused":  # the step ends when every gather has landed
             torch.cuda.current_stream().wait_stream(comm)
@@ -578,7 +599,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
                 "peak_source": f"{peaks.source} {'sustained' if sustained else 'burst'} cuBLAS bf16"}
     roof["traffic"] = None if (args.mx or mode != "single") else load_traffic(workload)
     nvlink = None
-    if mode in ("fused", "unfused"):
+    if mode in TP_MODES:
         # every GPU sends its slice of every output to each peer and receives the rest
         sent = sum(M * it["N"] * 2 * (world - 1) for it in items)
         recv = sum(M * (N - it["N"]) * 2 for it, (_, N, _) in zip(items, full))
@@ -606,7 +627,7 @@ def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -
     # adds its activation coder (and, for decode, the bf16 conversion)
     if args.mx:
         per_step = len(items) * (3 if decode else 2)
-    elif mode == "fused":
+    elif mode in ("fused", "ce"):
         per_step = len(items)
     else:
         per_step = sum(1 + (mx.workspace_bytes(M, it["N"], it["K"], "prepacked") > 0 and M >= 4) for it in items)
@@ -622,6 +643,8 @@ def parallelism_text(mode: str, world: int) -> str:
             "weak": f"weak x{world}: each rank its own N-slice of a {world}x wider layer, no collective",
             "fused": f"tp{world} column-parallel, all-gather fused into the GEMM epilogue (NVLink stores into every "
                      "GPU's full output)",
+            "ce": f"tp{world} column-parallel, local GEMM into the full output + copy-engine push of the slice "
+                  "to every peer over NVLink (overlapped with the next GEMM)",
             "unfused": f"tp{world} column-parallel, local GEMM + NCCL all-gather (each gather overlapped with "
                        "the next GEMM on a second stream)"}[mode]
 
@@ -676,7 +699,7 @@ def main():
         print(json.dumps({
             "metric": metric, "value": r["value"], "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_step"], "higher_is_better": True,
-            "scaling": "strong" if r["mode"] in ("fused", "unfused") else "weak", "vs_baseline": None,
+            "scaling": "strong" if r["mode"] in TP_MODES else "weak", "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) bf16 activations, N(0,0.02) OCP-MXFP4 weights)",
             "config": {

@@ -1029,6 +1029,17 @@ int mxfp4_ipc_close(void* dev_ptr, size_t offset) {
   return ret(cudaIpcCloseMemHandle(static_cast<char*>(dev_ptr) - offset));
 }
 
+int mxfp4_copy_columns(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                       int rows, void* stream) {
+  if (!dst || !src || rows < 0 || width_bytes > dst_pitch || width_bytes > src_pitch)
+    return MXFP4_ERR_INVALID_ARGUMENT;
+  if (rows == 0 || width_bytes == 0) return 0;
+  // One pitched copy on the stream: the copy engines move it (a peer's buffer goes over NVLink),
+  // no SM takes part, so it runs beside the kernels of other streams.
+  return ret(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, static_cast<size_t>(rows),
+                               cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+}
+
 
 }  // extern "C"
 

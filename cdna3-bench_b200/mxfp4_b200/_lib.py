@@ -45,6 +45,7 @@ EXPORTED = (
     "mxfp4_ipc_export",
     "mxfp4_ipc_open",
     "mxfp4_ipc_close",
+    "mxfp4_copy_columns",
     "mxfp4_mx_weight_bytes",
     "mxfp4_prepack_mx",
     "mxfp4_mx_workspace_bytes",
@@ -100,6 +101,7 @@ def _declare(lib):
         "mxfp4_ipc_export": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
         "mxfp4_ipc_open": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
         "mxfp4_ipc_close": (_I, [_P, _SZ]),
+        "mxfp4_copy_columns": (_I, [_P, _SZ, _P, _SZ, _SZ, _I, _P]),
         "mxfp4_mx_weight_bytes": (_SZ, [_I, _I]),
         "mxfp4_prepack_mx": (_I, [_P, _P, _I, _I, _I, _P, _P]),
         "mxfp4_mx_workspace_bytes": (_SZ, [_I, _I, _I, _I]),

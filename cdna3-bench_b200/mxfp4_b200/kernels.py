@@ -269,6 +269,16 @@ def ipc_close(ptr: int, offset: int) -> None:
     _lib.check(_lib.lib().mxfp4_ipc_close(ctypes.c_void_p(ptr), offset), "mxfp4_ipc_close")
 
 
+def copy_columns(dst_ptr: int, dst_pitch: int, src_ptr: int, src_pitch: int, width_bytes: int, rows: int,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """Pitched device-to-device copy of `rows` rows of `width_bytes` on `stream` (default: the
+    current stream) by the copy engines; `dst_ptr` may be a peer's buffer from :func:`ipc_open`."""
+    s = ctypes.c_void_p(stream.cuda_stream) if stream is not None else _stream()
+    _lib.check(_lib.lib().mxfp4_copy_columns(ctypes.c_void_p(int(dst_ptr)), dst_pitch, ctypes.c_void_p(int(src_ptr)),
+                                             src_pitch, width_bytes, rows, s),
+               "mxfp4_copy_columns")
+
+
 def _gemm_layout(A, B, Bs, C, layout: int, N: int, K: int, path: int, name: str):
     M = A.shape[0]
     if C is None:

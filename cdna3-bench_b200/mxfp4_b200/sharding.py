@@ -136,6 +136,21 @@ class PeerOutput:
             kk.ipc_close(p, o)
         self._opened = []
 
+    def push(self, n0: int, n1: int, streams=None):
+        """Copy this GPU's columns [n0, n1) of `buffer` into every peer's buffer with the copy
+        engines (one pitched copy per peer; `streams`: one CUDA stream per peer, else the current
+        stream).  No SM takes part, so the copies overlap kernels on other streams; `sync` after
+        them (ordered after the copies on every GPU) makes them visible to the peers."""
+        from . import kernels as kk
+
+        esz = self.buffer.element_size()
+        pitch = self.N * esz
+        src = self.ptrs[self.rank] + n0 * esz
+        peers = [r for r in range(self.world) if r != self.rank]
+        for i, r in enumerate(peers):
+            kk.copy_columns(self.ptrs[r] + n0 * esz, pitch, src, pitch, (n1 - n0) * esz, self.M,
+                            stream=streams[i] if streams else None)
+
     def sync(self):
         """Order this GPU's later work after every peer's stores into `buffer` (a stream-ordered
         all-reduce of one int: it completes only after every rank's preceding kernels)."""
@@ -153,5 +168,19 @@ def forward_fused(layer: "ColumnParallelMXFP4", A: torch.Tensor, out: PeerOutput
     if out.dtype not in (torch.bfloat16, torch.float32) or out.N != layer.N or out.M != A.shape[0]:
         raise ValueError("PeerOutput shape/dtype does not match the layer and A")
     kk.gemm_allgather(A, layer.weight, out.ptrs, layer.n0, layer.N, out_dtype=out.dtype)
+    out.sync()
+    return out.buffer
+
+
+def forward_copy_engine(layer: "ColumnParallelMXFP4", A: torch.Tensor, out: PeerOutput) -> torch.Tensor:
+    """Column-parallel GEMM whose slice is written straight into this GPU's full output and then
+    pushed to every peer by the copy engines (NVLink, no SMs), then one tiny collective orders
+    the reads.  Returns this GPU's full [M, N] output."""
+    from . import kernels as kk
+
+    if out.dtype not in (torch.bfloat16, torch.float32) or out.N != layer.N or out.M != A.shape[0]:
+        raise ValueError("PeerOutput shape/dtype does not match the layer and A")
+    kk.gemm_allgather(A, layer.weight, [out.ptrs[out.rank]], layer.n0, layer.N, out_dtype=out.dtype)
+    out.push(layer.n0, layer.n1)
     out.sync()
     return out.buffer

@@ -167,6 +167,15 @@ int mxfp4_ipc_export(const void* dev_ptr, void* handle_out, size_t* offset_out);
 int mxfp4_ipc_open(const void* handle, size_t offset, void** dev_ptr_out);
 int mxfp4_ipc_close(void* dev_ptr, size_t offset);
 
+/* Copy-engine form of the column all-gather (no reference counterpart): copies `rows` rows of
+ * width_bytes each from src (row pitch src_pitch) to dst (row pitch dst_pitch) as one pitched
+ * device-to-device copy on `stream`.  With dst a peer's output buffer (mxfp4_ipc_open) at this
+ * GPU's column offset, it pushes this GPU's output columns over NVLink without occupying any
+ * SM, so it overlaps the next GEMM on another stream.  The caller orders the peers' reads (a
+ * stream-ordered collective after the copies on every GPU). */
+int mxfp4_copy_columns(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width_bytes,
+                       int rows, void* stream);
+
 /* Fixed size of the device buffer mxfp4_gemm_noalloc uses in place of a workspace. */
 #define MXFP4_NOALLOC_SCRATCH_BYTES (32u << 20)
 

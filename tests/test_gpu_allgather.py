@@ -43,7 +43,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, how):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -60,7 +60,7 @@ def _rank(rank, world, port, q):
             out = sharding.PeerOutput(M, N, torch.float32)
             At = torch.from_numpy(A).cuda().to(torch.bfloat16)
             for _ in range(2):  # twice: the buffer is reused
-                Y = sharding.forward_fused(layer, At, out)
+                Y = getattr(sharding, how)(layer, At, out)
             torch.cuda.synchronize()
             res[M] = rel_err(Y.cpu().numpy(), o.ref_gemm(A, Bp, Bs))
             dist.barrier()
@@ -71,13 +71,16 @@ def _rank(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_fused_allgather_equals_unsharded():
+@pytest.mark.parametrize("how", ["forward_fused", "forward_copy_engine"])
+def test_two_gpu_fused_allgather_equals_unsharded(how):
+    """Both multi-GPU forms -- the all-gather fused into the epilogue, and the copy-engine push
+    after a local GEMM -- give every rank the unsharded product."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q, how)) for r in range(2)]
     for p in ps:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(2))
