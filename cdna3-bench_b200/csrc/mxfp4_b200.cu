@@ -207,10 +207,11 @@ int launch_tc_splitk(const void* A, const uint8_t* wpack, const OutSpec& o, int 
   const int blocks = static_cast<int>(std::min<size_t>(ceil_div(static_cast<int>(std::min<size_t>(work, 1u << 30)), 256),
                                                        static_cast<size_t>(d->sm_count) * 8));
   if (c_dtype == MXFP4_DTYPE_F32)
-    splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N, static_cast<float*>(o.dst[0]), o.ldc);
+    splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N, static_cast<float*>(o.dst[0]) + o.n_off,
+                                                            o.ldc);
   else
-    splitk_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N,
-                                                                    static_cast<__nv_bfloat16*>(o.dst[0]), o.ldc);
+    splitk_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+        ws, sp.splits, M, N, static_cast<__nv_bfloat16*>(o.dst[0]) + o.n_off, o.ldc);
   return launch_status();
 }
 
@@ -946,7 +947,8 @@ int gemm_impl(const void* A, const uint8_t* B, const uint8_t* B_scales, const Ou
     case MXFP4_PATH_TC_SMEM: {
       const SplitPlan sp = plan_splitk(M, N, K, d->sm_count);
       const size_t need = static_cast<size_t>(sp.splits) * M * N * 4;
-      if (sp.splits > 1 && C.count == 1 && C.n_off == 0 && rest && rest_bytes >= need && aligned16(rest)) {
+      if (sp.splits > 1 && C.count == 1 && C.n_off % 4 == 0 && C.ldc % 4 == 0 && rest && rest_bytes >= need &&
+          aligned16(rest)) {
         float* ws = reinterpret_cast<float*>(rest);
         return path == MXFP4_PATH_TC ? launch_tc_splitk<true>(A, wpack, C, c_dtype, M, N, K, sp, ws, s, d)
                                      : launch_tc_splitk<false>(A, wpack, C, c_dtype, M, N, K, sp, ws, s, d);

@@ -37,6 +37,28 @@ def test_multi_destination_single_gpu(M, path, dtype):
         assert (h[:, :n_off] == 7.0).all() and (h[:, n_off + N:] == 7.0).all()  # nothing outside the slice
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_single_destination_split_k_at_offset(dtype):
+    """One destination at a non-zero column offset on a shape with few tiles (3 tiles, K = 2048):
+    the large-M kernel splits K and the reduction writes the slice at n_off (the copy-engine
+    multi-GPU form runs every rank's GEMM this way)."""
+    import mxfp4_b200 as mx
+    from mxfp4_b200 import kernels as kk
+
+    M, N, K, ldc, n_off = 256, 384, 2048, 1024, 512
+    A, Bp, Bs = make_case(M, N, K, seed=5)
+    ref = o.ref_gemm(A, Bp, Bs)
+    w = mx.prepack_b200(Bp, Bs)
+    At = torch.from_numpy(A).cuda().to(torch.bfloat16)
+    buf = torch.full((M, ldc), 7.0, dtype=dtype, device="cuda")
+    kk.gemm_allgather(At, w, [buf.data_ptr()], n_off, ldc, out_dtype=dtype, path="tc")
+    torch.cuda.synchronize()
+    assert mx.device_error() == 0
+    h = buf.float().cpu().numpy()
+    assert rel_err(h[:, n_off:n_off + N], ref) <= 1e-2
+    assert (h[:, :n_off] == 7.0).all() and (h[:, n_off + N:] == 7.0).all()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
