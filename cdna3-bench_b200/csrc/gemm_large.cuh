@@ -421,10 +421,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // Sum of the split-K partials ws[splits][M][N] (fp32) into C (row stride ldc).  Four columns
-// per thread; N is a multiple of 4 on this path.
+// per thread; N is a multiple of 4 on this path.  Launched as a programmatic dependent of the
+// GEMM that writes the partials, so its launch overlaps the GEMM's tail.
 template <typename OutT>
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M, int N,
                                                             OutT* __restrict__ C, int ldc) {
+  griddep_wait();  // launched as the GEMM's programmatic dependent: its partials are complete here
   const size_t n4 = static_cast<size_t>(N) / 4;
   const size_t total = static_cast<size_t>(M) * n4;
   const size_t plane = static_cast<size_t>(M) * N;

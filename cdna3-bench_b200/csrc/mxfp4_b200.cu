@@ -126,12 +126,17 @@ struct OutSpec {
 struct SplitPlan {
   int splits, kbps;
 };
+int env_knob(const char* name);
 SplitPlan plan_splitk(int M, int N, int K, int sm_count) {
+  // tuning knobs (sweeps only): the most slices and the fewest K-blocks per slice
+  static const int max_knob = env_knob("MXFP4_TC_MAX_SPLITS"), kbps_knob = env_knob("MXFP4_TC_MIN_KBPS");
+  const int max_s = max_knob >= 1 && max_knob <= 16 ? max_knob : 8;
+  const int min_kbps = kbps_knob >= 1 && kbps_knob <= 64 ? kbps_knob : 8;
   const int tiles = ceil_div(M, kTcTileAct) * n_blocks_of(N);
   const int kb = k_blocks_of(K);
   SplitPlan p{1, kb};
   if (2 * tiles > sm_count || N % 4) return p;
-  int s = std::min({8, sm_count / tiles, kb / 8});
+  int s = std::min({max_s, sm_count / tiles, kb / min_kbps});
   if (s < 2) return p;
   p.kbps = ceil_div(kb, s);
   p.splits = ceil_div(kb, p.kbps);  // no empty slice
@@ -197,7 +202,11 @@ int launch_tc(const void* A, const uint8_t* wpack, const OutSpec& o, int M, int 
   return launch_status();
 }
 
-// Large-M kernel with split-K: fp32 partials into `ws`, then one reduction into C.
+template <typename... KArgs, typename... Args>
+int launch_pdl_grid(void (*kernel)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t stream, Args... args);
+
+// Large-M kernel with split-K: fp32 partials into `ws`, then one reduction into C (a
+// programmatic dependent launch: it waits for the GEMM's partials with griddepcontrol.wait).
 template <bool kTS>
 int launch_tc_splitk(const void* A, const uint8_t* wpack, const OutSpec& o, int c_dtype, int M, int N, int K,
                      const SplitPlan& sp, float* ws, cudaStream_t stream, DeviceState* d) {
@@ -207,12 +216,11 @@ int launch_tc_splitk(const void* A, const uint8_t* wpack, const OutSpec& o, int 
   const int blocks = static_cast<int>(std::min<size_t>(ceil_div(static_cast<int>(std::min<size_t>(work, 1u << 30)), 256),
                                                        static_cast<size_t>(d->sm_count) * 8));
   if (c_dtype == MXFP4_DTYPE_F32)
-    splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(ws, sp.splits, M, N, static_cast<float*>(o.dst[0]) + o.n_off,
-                                                            o.ldc);
-  else
-    splitk_reduce_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
-        ws, sp.splits, M, N, static_cast<__nv_bfloat16*>(o.dst[0]) + o.n_off, o.ldc);
-  return launch_status();
+    return launch_pdl_grid(splitk_reduce_kernel<float>, dim3(blocks), 256, 0, stream, static_cast<const float*>(ws),
+                           sp.splits, M, N, static_cast<float*>(o.dst[0]) + o.n_off, o.ldc);
+  return launch_pdl_grid(splitk_reduce_kernel<__nv_bfloat16>, dim3(blocks), 256, 0, stream,
+                         static_cast<const float*>(ws), sp.splits, M, N,
+                         static_cast<__nv_bfloat16*>(o.dst[0]) + o.n_off, o.ldc);
 }
 
 // ------------------------------------------------------------------ small-M launch
