@@ -362,6 +362,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_tile(t, m_blocks, n_blocks, k_blocks, kbps, mb, nb, kb_lo, kb_hi, ks);
       for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
         if ((it & 1) == static_cast<uint32_t>(grp)) {
+          // With an odd stage count the two groups take turns on each stage, so a group waits on
+          // every second phase of full[s], always with the same parity -- and a parity wait cannot
+          // tell its own phase from the one two back while the other group's load of the phase
+          // between is still in flight.  So first wait until the other group has finished that
+          // phase (dqd[s] of iteration it - S: unambiguous, since its next phase needs this
+          // group's own arrival); after it, the parity wait on full[s] names exactly one phase.
+          if (it >= static_cast<uint32_t>(S) && !warp_wait(&dqd[s], ph ^ 1, kErrWaitDequant, abort_flag)) {
+            aborted = true;
+            break;
+          }
           if (!warp_wait(&full[s], ph, kErrWaitFull, abort_flag)) {
             aborted = true;
             break;
