@@ -28,8 +28,8 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
   [M, N] output and the copy engines push the slice into every peer's output over NVLink (one
   pitched copy per peer, CUDA IPC buffers) while the next GEMM computes; one stream-ordered
   one-int NCCL all-reduce per step orders the reads.  `--fused` stores every tile into all GPUs'
-  outputs from the GEMM epilogue instead (with many destinations an occasional call stalls until
-  the kernels' bounded waits give up, so it is opt-in); `--unfused` uses an NCCL all-gather per
+  outputs from the GEMM epilogue instead (opt-in; faster at 2 and 4 GPUs, not yet measured at 8
+  since the fix of the race that made it stall on rare calls); `--unfused` uses an NCCL all-gather per
   GEMM.  tp_sweep is BASELINE configs[4] in the same form.
 """
 
@@ -94,7 +94,7 @@ def parse(argv=None):
                     help="N > 1: GEMM then a separate NCCL all-gather on a second stream")
     ap.add_argument("--fused", action="store_true",
                     help="N > 1: the all-gather fused into the GEMM epilogue, stores straight into every GPU's "
-                         "output over NVLink (faster; with many destinations it stalls on rare calls, see DESIGN)")
+                         "output over NVLink")
     ap.add_argument("--ce", action="store_true",
                     help="N > 1 (the default): each GEMM writes its slice into this GPU's full output and the "
                          "copy engines push it to every peer over NVLink while the next GEMM computes")
