@@ -27,10 +27,9 @@ bf16 output, fp32 accumulation.  One step = the four GEMMs.  Synthetic, seeded d
   split over the ranks in whole 128-row tiles; each GEMM writes its slice into this GPU's full
   [M, N] output and the copy engines push the slice into every peer's output over NVLink (one
   pitched copy per peer, CUDA IPC buffers) while the next GEMM computes; one stream-ordered
-  one-int NCCL all-reduce per step orders the reads.  `--fused` stores every tile into all GPUs'
-  outputs from the GEMM epilogue instead (opt-in; faster at 2 and 4 GPUs, not yet measured at 8
-  since the fix of the race that made it stall on rare calls); `--unfused` uses an NCCL all-gather per
-  GEMM.  tp_sweep is BASELINE configs[4] in the same form.
+  one-int NCCL all-reduce per step orders the reads; this is the default at 2 GPUs (`--ce`).
+  `--fused`, the default at 4 and 8 GPUs, stores every tile into all GPUs' outputs from the GEMM
+  epilogue instead; `--unfused` uses an NCCL all-gather per GEMM.  tp_sweep is BASELINE configs[4] in the same form.
 """
 
 from __future__ import annotations
@@ -93,10 +92,10 @@ def parse(argv=None):
     ap.add_argument("--unfused", action="store_true",
                     help="N > 1: GEMM then a separate NCCL all-gather on a second stream")
     ap.add_argument("--fused", action="store_true",
-                    help="N > 1: the all-gather fused into the GEMM epilogue, stores straight into every GPU's "
+                    help="N > 1 (the default at 4 and 8 GPUs): the all-gather fused into the GEMM epilogue, stores straight into every GPU's "
                          "output over NVLink")
     ap.add_argument("--ce", action="store_true",
-                    help="N > 1 (the default): each GEMM writes its slice into this GPU's full output and the "
+                    help="N > 1 (the default at 2 GPUs): each GEMM writes its slice into this GPU's full output and the "
                          "copy engines push it to every peer over NVLink while the next GEMM computes")
     ap.add_argument("--no-graph", action="store_true",
                     help="decode and c0 workloads: launch each GEMM from Python instead of replaying a CUDA graph per step")
@@ -381,7 +380,13 @@ def tp_mode(args, ctx, workload: str) -> str:
         return "weak"
     if args.unfused:
         return "unfused"
-    return "fused" if args.fused else "ce"
+    if args.fused:
+        return "fused"
+    if args.ce:
+        return "ce"
+    # Measured on B200 (20 steps, flux_ds): the copy-engine push leads at 2 GPUs (1907 vs 1880
+    # TFLOP/s), the fused epilogue at 4 (1945 vs 1712) and 8 (1694 vs 1306).
+    return "fused" if ctx.world >= 4 else "ce"
 
 
 def measure(args, ctx, workload: str, steps: int, warmup: int, want_e2e: bool) -> dict:
